@@ -1,0 +1,123 @@
+/*
+ * h3b.h -- C ABI of libh3b.so, the B200-native (sm_100a) W4A8 ConvRot quantised linear.
+ *
+ * Every pointer argument is a device pointer unless the name ends in `_host`.  The caller owns every buffer, including
+ * outputs and scratch ("workspace"): no entry point allocates device memory.  Work is enqueued on `stream` (a
+ * cudaStream_t; NULL means the legacy default stream) and the call returns without synchronising.  Weight tensors may be
+ * views into a larger byte buffer (256-byte aligned rows are enough).
+ *
+ * Return value: H3B_OK (0) or a positive H3B_ERR_* code; h3b_last_error() then returns a message (thread-local, valid
+ * until the next call on the same thread).  H3B_ERR_ARG means the arguments are invalid (the Python layer raises
+ * ValueError); every other code is a device or build failure (RuntimeError).
+ *
+ * Numerics (all entry points): identical to the reference's "ck" profile of h3turbo/h3/qlinear.py.  The int4->int8 decode,
+ * the int32 accumulation and every epilogue rounding are bit-exact; the only float step that is not the reference's
+ * correctly rounded fp64 computation is the ConvRot rotation, done as an fp32 fast Walsh-Hadamard transform.
+ *
+ * Reference interfaces named below are file:line in the reference project (Alexpoopy1/MiniMax-H3-Turbo).
+ */
+#ifndef H3B_H
+#define H3B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define H3B_ABI_VERSION 1
+
+enum h3b_status {
+  H3B_OK = 0,
+  H3B_ERR_ARG = 1,          /* invalid argument (shape, dtype, size, alignment) */
+  H3B_ERR_CUDA = 2,         /* a CUDA runtime call failed */
+  H3B_ERR_UNSUPPORTED = 3,  /* valid for the reference, not supported by this build (e.g. convrot 1024) */
+  H3B_ERR_DEVICE = 4        /* a kernel reported a failure (a bounded wait timed out); see h3b_device_error */
+};
+
+enum h3b_dtype {
+  H3B_BF16 = 0,
+  H3B_FP16 = 1,
+  H3B_FP32 = 2,
+  H3B_FP8_E4M3 = 3, /* float8_e4m3fn group scales (raw bytes) */
+  H3B_INT32 = 4     /* int32 accumulator output (parity dump) */
+};
+
+enum h3b_quant_mode {
+  H3B_QMODE_CK = 0,    /* absmax of the unrounded rotation; epilogue (acc * xs) * s_ch   (qlinear.py:278-283, :400-401) */
+  H3B_QMODE_EAGER = 1  /* absmax of the dtype-rounded rotation; epilogue acc * (xs * s_ch) (qlinear.py:284-287, :402-403) */
+};
+
+/* ABI version (H3B_ABI_VERSION) and the last error message of this thread. */
+int h3b_version(void);
+const char* h3b_last_error(void);
+
+/* Rotate + per-token int8 quantisation of activations (kernel KA).
+ * Replaces quantize_activation / _quantize_rows (qlinear.py:267-303), the activation half of comfy_kitchen's fused
+ * w4a8_int8_linear reached through _run_ck (qlinear.py:427-429).
+ *   x      [M, ldx] of x_dtype (bf16/fp16/fp32); the row holds K features, or [gate | up] (2K) when swiglu != 0
+ *          (input_act="swiglu", qlinear.py:376-379: silu(gate) * up in x_dtype, applied before the rotation).
+ *   convrot 4, 16, 64 or 256 (the ConvRot block; K % convrot == 0).
+ *   q      [M, ldq] int8 codes out; xs [M] fp32 per-row scales out. */
+int h3b_rotq(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int convrot, int swiglu, int quant_mode,
+             int8_t* q, int64_t ldq, float* xs, void* stream);
+
+/* Block rotation only: y = per-convrot-block x @ H in y_dtype (one rounding of the fp32 transform).
+ * Replaces rotate (qlinear.py:118-132). */
+int h3b_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int convrot, void* y, int y_dtype,
+               int64_t ldy, void* stream);
+
+/* int4 codebook indices + group scales -> the exact int8 grid [N, K] (row stride ldg bytes).
+ * Replaces decode_int8_grid / _decode_rows / _pair_lut (qlinear.py:157-204).
+ *   q4     [N, ldq4 bytes] packed nibbles, low nibble first (types.py:14-16)
+ *   s_rel  [N, lds elements] of s_dtype (fp8 e4m3 bytes, fp16, bf16 or fp32), K / group per row
+ *   codebook fp32 [16]; group >= 4 dividing 16 or a multiple of 16 (qlinear.py:146). */
+int h3b_decode_grid(const void* q4, int64_t N, int64_t K, int64_t ldq4, const void* s_rel, int s_dtype, int64_t lds,
+                    const float* codebook, int group, int8_t* grid, int64_t ldg, void* stream);
+
+/* Exact int32 a[M, K] @ b[N, K]^T for int8 operands on the tcgen05 tensor cores (parity of the integer accumulator).
+ * Replaces _int8_mm (qlinear.py:236-254).  lda/ldb in bytes (multiples of 16), ldc in elements. */
+int h3b_int8_gemm_s32(const int8_t* a, int64_t lda, int64_t M, const int8_t* b, int64_t ldb, int64_t N, int64_t K,
+                      int32_t* c, int64_t ldc, void* stream);
+
+/* Scratch bytes h3b_w4a8_gemm / h3b_w4a8_linear need for these sizes (0 is a valid answer). */
+size_t h3b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+size_t h3b_linear_workspace_bytes(int64_t M, int64_t N, int64_t K);
+
+/* W4A8 GEMM + epilogue on already-quantised activation codes (kernel KB).
+ * Replaces the int8 GEMM and epilogue of _TorchRunner._a8 (qlinear.py:396-405):
+ *   out = out_dtype( (fp32(acc) * xs[m]) * s_ch[n] )            quant_mode CK
+ *   out = out_dtype(  fp32(acc) * (xs[m] * s_ch[n]) )           quant_mode EAGER
+ *   out = out_dtype( fp32(out) + fp32(bias[n]) )                 when bias != NULL (bias already of out_dtype)
+ * out_dtype H3B_INT32 stores the raw accumulator instead (xs, s_ch, bias ignored).
+ *   qa [M, lda bytes] int8 codes, xs [M] fp32; weight as in h3b_decode_grid; out [M, ldo elements]. */
+int h3b_w4a8_gemm(const int8_t* qa, int64_t lda, const float* xs, int64_t M, const void* q4, int64_t ldq4,
+                  const void* s_rel, int s_dtype, int64_t lds, const float* s_ch, const float* codebook, int group,
+                  const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N, int64_t K, int quant_mode,
+                  void* workspace, size_t ws_bytes, void* stream);
+
+/* GEMM + epilogue on an already-decoded int8 weight grid [N, ldg bytes] (same epilogue contract as h3b_w4a8_gemm).
+ * For callers that keep decoded grids resident (weights that never stream); no workspace.  Same reference lines as
+ * h3b_w4a8_gemm (qlinear.py:396-405) with the decode (qlinear.py:194-204) hoisted out. */
+int h3b_int8_gemm_epilogue(const int8_t* qa, int64_t lda, const float* xs, int64_t M, const int8_t* grid, int64_t ldg,
+                           const float* s_ch, const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N,
+                           int64_t K, int quant_mode, void* stream);
+
+/* The whole W4A8 linear: (swiglu) -> rotate+quantise -> GEMM -> epilogue.  The seam the reference hands to
+ * comfy_kitchen: _run_ck -> w4a8_int8_linear(x2, w.q, s_rel, w.s_ch, codebook, bias, group_size, convrot_groupsize,
+ * out_dtype) (qlinear.py:427-429, result contract :446-451).  workspace >= h3b_linear_workspace_bytes(M, N, K). */
+int h3b_w4a8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int swiglu, const void* q4,
+                    int64_t ldq4, const void* s_rel, int s_dtype, int64_t lds, const float* s_ch, const float* codebook,
+                    int group, int convrot, const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N,
+                    int quant_mode, void* workspace, size_t ws_bytes, void* stream);
+
+/* Device-side failure flag of the current device: a kernel whose bounded wait ran out sets it (and returns instead of
+ * hanging).  Returns the flag and, when clear != 0, resets it.  Synchronises the device. */
+int h3b_device_error(int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3B_H */

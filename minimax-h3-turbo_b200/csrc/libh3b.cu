@@ -1,0 +1,226 @@
+// libh3b.so: the C ABI declared in include/h3b.h, argument validation, error state, and the kernels (one translation
+// unit, so the device failure flag is a single symbol shared by every kernel).
+#include <cstdio>
+#include <string>
+
+#include "h3b_common.cuh"
+
+namespace h3b {
+
+static thread_local std::string g_err;
+
+void set_error(const std::string& msg) { g_err = msg; }
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  g_err = std::string(what) + ": " + cudaGetErrorString(e);
+  return H3B_ERR_CUDA;
+}
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return H3B_OK;
+}
+
+}  // namespace h3b
+
+#include "decode.cuh"
+#include "gemm_sm100.cuh"
+#include "rotq.cuh"
+
+namespace h3b {
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+static size_t act_size(int dt) { return dt == H3B_FP32 ? 4 : 2; }
+static bool is_act(int dt) { return dt == H3B_BF16 || dt == H3B_FP16 || dt == H3B_FP32; }
+static bool is_scale(int dt) { return dt == H3B_FP8_E4M3 || is_act(dt); }
+static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// qlinear.py:146 -- K divisible by 16, group and convrot; group >= 4 dividing 16 or a multiple of 16.
+static int check_weight_geometry(int64_t K, int group) {
+  if (group < 4 || K % 16 || K % group || ((16 % group) && (group % 16)))
+    return fail(H3B_ERR_ARG, "K=" + std::to_string(K) + " must be divisible by 16 and group_size=" + std::to_string(group) +
+                                 "; group_size >= 4 dividing 16 or a multiple of 16");
+  return H3B_OK;
+}
+
+static int check_rotq_args(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int convrot, int swiglu) {
+  if (!is_act(x_dtype)) return fail(H3B_ERR_ARG, "activation dtype must be bf16, fp16 or fp32");
+  if (M < 0 || K <= 0) return fail(H3B_ERR_ARG, "M must be >= 0 and K > 0");
+  if (convrot != 4 && convrot != 16 && convrot != 64 && convrot != 256) {
+    int n = convrot;
+    while (n > 1 && n % 4 == 0) n /= 4;
+    if (convrot < 4 || n != 1)
+      return fail(H3B_ERR_ARG, "regular Hadamard size must be a power of 4 (>= 4), got " + std::to_string(convrot));
+    return fail(H3B_ERR_UNSUPPORTED, "convrot " + std::to_string(convrot) + " is not supported by the b200 backend (4, 16, 64, 256)");
+  }
+  if (K % convrot) return fail(H3B_ERR_ARG, "last dim " + std::to_string(K) + " is not a multiple of the rotation block " + std::to_string(convrot));
+  if (K % 16) return fail(H3B_ERR_ARG, "K must be a multiple of 16");
+  if (K / 16 > 1024) return fail(H3B_ERR_UNSUPPORTED, "K > 16384 is not supported by the rotate+quantise kernel");
+  if (M > 0x7FFFFFFF) return fail(H3B_ERR_UNSUPPORTED, "M >= 2^31 rows");
+  const int64_t row_elems = swiglu ? 2 * K : K;
+  if (ldx < row_elems) return fail(H3B_ERR_ARG, "ldx is smaller than the row width");
+  if (!aligned(x, 16) || (ldx * static_cast<int64_t>(act_size(x_dtype))) % 16)
+    return fail(H3B_ERR_ARG, "x must be 16-byte aligned with a row stride that is a multiple of 16 bytes");
+  return H3B_OK;
+}
+
+static int check_weight_args(const void* q4, int64_t N, int64_t K, int64_t ldq4, const void* s_rel, int s_dtype,
+                             int64_t lds, const float* codebook, int group) {
+  if (N < 0) return fail(H3B_ERR_ARG, "N must be >= 0");
+  int rc = check_weight_geometry(K, group);
+  if (rc) return rc;
+  if (!is_scale(s_dtype)) return fail(H3B_ERR_ARG, "group scale dtype must be fp8_e4m3, fp16, bf16 or fp32");
+  if (ldq4 < K / 2 || ldq4 % 8 || !aligned(q4, 8)) return fail(H3B_ERR_ARG, "q must be 8-byte aligned with a row stride >= K/2 and a multiple of 8 bytes");
+  if (lds < K / group) return fail(H3B_ERR_ARG, "s_rel row stride is smaller than K / group_size");
+  if (!s_rel || !codebook) return fail(H3B_ERR_ARG, "s_rel and codebook must be given");
+  return H3B_OK;
+}
+
+}  // namespace h3b
+
+using namespace h3b;
+
+extern "C" {
+
+int h3b_version(void) { return H3B_ABI_VERSION; }
+
+const char* h3b_last_error(void) { return g_err.c_str(); }
+
+int h3b_rotq(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int convrot, int swiglu, int quant_mode,
+             int8_t* q, int64_t ldq, float* xs, void* stream) {
+  int rc = check_rotq_args(x, x_dtype, M, K, ldx, convrot, swiglu);
+  if (rc) return rc;
+  if (quant_mode != H3B_QMODE_CK && quant_mode != H3B_QMODE_EAGER) return fail(H3B_ERR_ARG, "quant_mode must be 'ck' or 'eager'");
+  if (ldq < K || ldq % 16 || !aligned(q, 16)) return fail(H3B_ERR_ARG, "q must be 16-byte aligned with a row stride >= K, multiple of 16");
+  if (M == 0) return H3B_OK;
+  return rotq_launch(x, x_dtype, M, K, ldx, convrot, swiglu, quant_mode, q, ldq, xs, nullptr, 0, 0,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int h3b_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int convrot, void* y, int y_dtype,
+               int64_t ldy, void* stream) {
+  int rc = check_rotq_args(x, x_dtype, M, K, ldx, convrot, 0);
+  if (rc) return rc;
+  if (!is_act(y_dtype)) return fail(H3B_ERR_ARG, "output dtype must be bf16, fp16 or fp32");
+  if (ldy < K) return fail(H3B_ERR_ARG, "ldy is smaller than K");
+  if (M == 0) return H3B_OK;
+  return rotq_launch(x, x_dtype, M, K, ldx, convrot, 0, MODE_ROTATE, nullptr, 0, nullptr, y, y_dtype, ldy,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int h3b_decode_grid(const void* q4, int64_t N, int64_t K, int64_t ldq4, const void* s_rel, int s_dtype, int64_t lds,
+                    const float* codebook, int group, int8_t* grid, int64_t ldg, void* stream) {
+  int rc = check_weight_args(q4, N, K, ldq4, s_rel, s_dtype, lds, codebook, group);
+  if (rc) return rc;
+  if (ldg < K || ldg % 16 || !aligned(grid, 16)) return fail(H3B_ERR_ARG, "grid must be 16-byte aligned with a row stride >= K, multiple of 16");
+  return decode_launch(q4, N, K, ldq4, s_rel, s_dtype, lds, codebook, group, grid, ldg, static_cast<cudaStream_t>(stream));
+}
+
+int h3b_int8_gemm_s32(const int8_t* a, int64_t lda, int64_t M, const int8_t* b, int64_t ldb, int64_t N, int64_t K,
+                      int32_t* c, int64_t ldc, void* stream) {
+  if (M < 0 || N < 0 || K <= 0 || K % 16) return fail(H3B_ERR_ARG, "need M, N >= 0 and K a positive multiple of 16");
+  if (lda < K || ldb < K || lda % 16 || ldb % 16 || !aligned(a, 16) || !aligned(b, 16))
+    return fail(H3B_ERR_ARG, "a and b must be 16-byte aligned with row strides >= K, multiples of 16 bytes");
+  if (ldc < N) return fail(H3B_ERR_ARG, "ldc is smaller than N");
+  if (M == 0 || N == 0) return H3B_OK;
+  return gemm_launch(a, lda, b, ldb, nullptr, nullptr, nullptr, c, H3B_INT32, ldc, M, N, K, H3B_QMODE_CK,
+                     static_cast<cudaStream_t>(stream));
+}
+
+size_t h3b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  (void)M;
+  return round_up(static_cast<size_t>(N) * static_cast<size_t>(K), 256);  // the decoded int8 grid
+}
+
+size_t h3b_linear_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  return round_up(static_cast<size_t>(M) * static_cast<size_t>(K), 256)  // activation codes
+         + round_up(static_cast<size_t>(M) * 4, 256)                    // per-row scales
+         + h3b_gemm_workspace_bytes(M, N, K);
+}
+
+int h3b_w4a8_gemm(const int8_t* qa, int64_t lda, const float* xs, int64_t M, const void* q4, int64_t ldq4,
+                  const void* s_rel, int s_dtype, int64_t lds, const float* s_ch, const float* codebook, int group,
+                  const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N, int64_t K, int quant_mode,
+                  void* workspace, size_t ws_bytes, void* stream) {
+  int rc = check_weight_args(q4, N, K, ldq4, s_rel, s_dtype, lds, codebook, group);
+  if (rc) return rc;
+  if (M < 0) return fail(H3B_ERR_ARG, "M must be >= 0");
+  if (out_dtype != H3B_BF16 && out_dtype != H3B_FP16 && out_dtype != H3B_FP32 && out_dtype != H3B_INT32)
+    return fail(H3B_ERR_ARG, "out dtype must be bf16, fp16, fp32 or int32");
+  if (quant_mode != H3B_QMODE_CK && quant_mode != H3B_QMODE_EAGER) return fail(H3B_ERR_ARG, "quant_mode must be 'ck' or 'eager'");
+  if (lda < K || lda % 16 || !aligned(qa, 16)) return fail(H3B_ERR_ARG, "activation codes must be 16-byte aligned with a row stride >= K, multiple of 16");
+  if (ldo < N) return fail(H3B_ERR_ARG, "ldo is smaller than N");
+  if (out_dtype != H3B_INT32 && (!s_ch || !xs)) return fail(H3B_ERR_ARG, "xs and s_ch must be given");
+  if (M == 0 || N == 0) return H3B_OK;
+  const size_t need = h3b_gemm_workspace_bytes(M, N, K);
+  if (!workspace || ws_bytes < need || !aligned(workspace, 256))
+    return fail(H3B_ERR_ARG, "workspace must be 256-byte aligned and hold h3b_gemm_workspace_bytes() = " + std::to_string(need) + " bytes");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int8_t* grid = static_cast<int8_t*>(workspace);
+  rc = decode_launch(q4, N, K, ldq4, s_rel, s_dtype, lds, codebook, group, grid, K, st);
+  if (rc) return rc;
+  return gemm_launch(qa, lda, grid, K, xs, s_ch, bias, out, out_dtype, ldo, M, N, K, quant_mode, st);
+}
+
+int h3b_int8_gemm_epilogue(const int8_t* qa, int64_t lda, const float* xs, int64_t M, const int8_t* grid, int64_t ldg,
+                           const float* s_ch, const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N,
+                           int64_t K, int quant_mode, void* stream) {
+  if (M < 0 || N < 0 || K <= 0 || K % 16) return fail(H3B_ERR_ARG, "need M, N >= 0 and K a positive multiple of 16");
+  if (out_dtype != H3B_BF16 && out_dtype != H3B_FP16 && out_dtype != H3B_FP32 && out_dtype != H3B_INT32)
+    return fail(H3B_ERR_ARG, "out dtype must be bf16, fp16, fp32 or int32");
+  if (quant_mode != H3B_QMODE_CK && quant_mode != H3B_QMODE_EAGER) return fail(H3B_ERR_ARG, "quant_mode must be 'ck' or 'eager'");
+  if (lda < K || ldg < K || lda % 16 || ldg % 16 || !aligned(qa, 16) || !aligned(grid, 16))
+    return fail(H3B_ERR_ARG, "codes and grid must be 16-byte aligned with row strides >= K, multiples of 16 bytes");
+  if (ldo < N) return fail(H3B_ERR_ARG, "ldo is smaller than N");
+  if (out_dtype != H3B_INT32 && (!s_ch || !xs)) return fail(H3B_ERR_ARG, "xs and s_ch must be given");
+  if (M == 0 || N == 0) return H3B_OK;
+  return gemm_launch(qa, lda, grid, ldg, xs, s_ch, bias, out, out_dtype, ldo, M, N, K, quant_mode,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int h3b_w4a8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int swiglu, const void* q4,
+                    int64_t ldq4, const void* s_rel, int s_dtype, int64_t lds, const float* s_ch, const float* codebook,
+                    int group, int convrot, const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N,
+                    int quant_mode, void* workspace, size_t ws_bytes, void* stream) {
+  int rc = check_rotq_args(x, x_dtype, M, K, ldx, convrot, swiglu);
+  if (rc) return rc;
+  rc = check_weight_args(q4, N, K, ldq4, s_rel, s_dtype, lds, codebook, group);
+  if (rc) return rc;
+  if (out_dtype != H3B_BF16 && out_dtype != H3B_FP16 && out_dtype != H3B_FP32)
+    return fail(H3B_ERR_ARG, "out dtype must be bf16, fp16 or fp32");
+  if (quant_mode != H3B_QMODE_CK && quant_mode != H3B_QMODE_EAGER) return fail(H3B_ERR_ARG, "quant_mode must be 'ck' or 'eager'");
+  if (ldo < N) return fail(H3B_ERR_ARG, "ldo is smaller than N");
+  if (!s_ch) return fail(H3B_ERR_ARG, "s_ch must be given");
+  if (M == 0 || N == 0) return H3B_OK;
+  const size_t need = h3b_linear_workspace_bytes(M, N, K);
+  if (!workspace || ws_bytes < need || !aligned(workspace, 256))
+    return fail(H3B_ERR_ARG, "workspace must be 256-byte aligned and hold h3b_linear_workspace_bytes() = " + std::to_string(need) + " bytes");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  int8_t* qa = reinterpret_cast<int8_t*>(ws);
+  float* xs = reinterpret_cast<float*>(ws + round_up(static_cast<size_t>(M) * K, 256));
+  char* rest = ws + round_up(static_cast<size_t>(M) * K, 256) + round_up(static_cast<size_t>(M) * 4, 256);
+  rc = rotq_launch(x, x_dtype, M, K, ldx, convrot, swiglu, quant_mode, qa, K, xs, nullptr, 0, 0, st);
+  if (rc) return rc;
+  return h3b_w4a8_gemm(qa, K, xs, M, q4, ldq4, s_rel, s_dtype, lds, s_ch, codebook, group, bias, out, out_dtype, ldo, N,
+                       K, quant_mode, rest, ws_bytes - static_cast<size_t>(rest - ws), stream);
+}
+
+int h3b_device_error(int clear) {
+  unsigned int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return -static_cast<int>(cuda_fail(e, "cudaDeviceSynchronize"));
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
+  if (e != cudaSuccess) return -static_cast<int>(cuda_fail(e, "cudaMemcpyFromSymbol"));
+  if (clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) return -static_cast<int>(cuda_fail(e, "cudaMemcpyToSymbol"));
+  }
+  return static_cast<int>(v);
+}
+
+}  // extern "C"

@@ -1,0 +1,57 @@
+"""Seeded synthetic W4A8 layers and activations for benchmarks, built on the GPU with torch.
+
+The benchmark configurations quote "symmetric int4, group 128, fp16 scales, then ConvRot" weights; this maps that onto
+the reference's W4A8Weight format (types.py:10-47):
+  1. W ~ N(0, 0.02) fp32 [N, K]
+  2. W_rot = W @ H per 256-block (the ConvRot basis; H is symmetric and involutory)
+  3. per (row, 128-group): sc = max|W_rot| / 7, code = clamp(rint(W_rot / sc), -7, 7), nibble = code + 8, codebook i - 8
+  4. s_ch[n] = max_g sc[n, g] * 7 / 127 (fp32), s_rel = fp16(sc / s_ch), so |codebook * s_rel| reaches ~127
+  5. q[n, j] = nibble[n, 2j] | nibble[n, 2j + 1] << 4
+Activations: x ~ N(0, 1) with a fraction of outlier channels scaled x20, cast to bf16.  Generation is chunked over rows
+so 13824 x 27648 layers need no more than a few hundred MB of temporaries.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .qlinear import hadamard_regular
+from .types import W4A8Weight
+
+
+@torch.no_grad()
+def synthetic_w4a8(n: int, k: int, *, group: int = 128, convrot: int = 256, seed: int = 0, device="cuda",
+                   rows_per_chunk: int = 2048) -> W4A8Weight:
+    if k % group or k % convrot:
+        raise ValueError("K must be a multiple of the group size and the ConvRot block")
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    h = hadamard_regular(convrot, dev, torch.float32)
+    q = torch.empty(n, k // 2, dtype=torch.int8, device=dev)
+    s_rel = torch.empty(n, k // group, dtype=torch.float16, device=dev)
+    s_ch = torch.empty(n, dtype=torch.float32, device=dev)
+    for r0 in range(0, n, rows_per_chunk):
+        r1 = min(n, r0 + rows_per_chunk)
+        w = torch.randn(r1 - r0, k, generator=gen, device=dev) * 0.02
+        w_rot = (w.view(r1 - r0, k // convrot, convrot) @ h).view(r1 - r0, k // group, group)
+        sc = (w_rot.abs().amax(-1) / 7.0).clamp_min(1e-12)
+        code = torch.clamp(torch.round(w_rot / sc[..., None]), -7, 7).to(torch.int32).view(r1 - r0, k) + 8
+        ch = sc.amax(-1) * (7.0 / 127.0)
+        s_ch[r0:r1] = ch
+        s_rel[r0:r1] = (sc / ch[:, None]).to(torch.float16)
+        q[r0:r1] = (code[:, 0::2] | (code[:, 1::2] << 4)).to(torch.uint8).view(torch.int8)
+    codebook = torch.arange(16, dtype=torch.float32, device=dev) - 8.0
+    return W4A8Weight(q, s_rel, s_ch, codebook, group_size=group, convrot=convrot)
+
+
+@torch.no_grad()
+def synthetic_activation(m: int, k: int, *, outlier_frac: float = 0.005, n_outliers: Optional[int] = None, seed: int = 0,
+                         dtype: torch.dtype = torch.bfloat16, device="cuda") -> torch.Tensor:
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed + 1000)
+    x = torch.randn(m, k, generator=gen, device=dev, dtype=torch.float32)
+    cnt = n_outliers if n_outliers is not None else max(1, round(outlier_frac * k))
+    ch = torch.randperm(k, generator=gen, device=dev)[:cnt]
+    x[:, ch] *= 20.0
+    return x.to(dtype)

@@ -34,8 +34,9 @@ DTYPES = ("bf16", "fp16", "fp32")
 def bf16_bits_from_f32(a: np.ndarray) -> np.ndarray:
     """fp32 -> bf16 bit pattern, round to nearest even; NaN stays a quiet NaN (torch's c10::BFloat16 rounding)."""
     a = np.ascontiguousarray(a, dtype=np.float32)
-    u = a.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    u = a.view(np.uint32)
+    with np.errstate(over="ignore"):
+        r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)  # wraps only for NaN payloads, fixed below
     nan = np.isnan(a)
     if nan.any():
         r = np.where(nan, np.uint16(0x7FC0), r)
