@@ -112,6 +112,22 @@ int h3b_w4a8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld
                     int group, int convrot, const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N,
                     int quant_mode, void* workspace, size_t ws_bytes, void* stream);
 
+/* Allocation-free W4A8 GEMM + epilogue: h3b_w4a8_gemm without the workspace argument.  No counterpart in the
+ * reference.  For callers that cannot allocate device memory: code running inside a host framework or plugin that
+ * gives it no device allocator, a C/FFI caller with no CUDA memory pool of its own, or a latency-critical loop that must
+ * not call cudaMalloc (it can synchronise the whole device).  The decoded weight rows live in one file-scope device
+ * array of H3B_NOALLOC_SCRATCH_BYTES that every GPU using the library holds until the process exits; the weight is
+ * decoded and multiplied in slabs of rows that fit in it, so any N works, and K may be at most
+ * H3B_NOALLOC_SCRATCH_BYTES / 32 (larger K is rejected with H3B_ERR_ARG).  The first call on a device looks up the
+ * array's device address (once per device); make that first call before any stream capture.  All calls share the one
+ * array: calls that may overlap on the GPU (different streams, or different host threads) race on it and must be
+ * serialised by the caller.  Nothing in it needs to start at zero (each slab is fully rewritten before it is read). */
+#define H3B_NOALLOC_SCRATCH_BYTES (16u << 20)
+int h3b_w4a8_gemm_noalloc(const int8_t* qa, int64_t lda, const float* xs, int64_t M, const void* q4, int64_t ldq4,
+                          const void* s_rel, int s_dtype, int64_t lds, const float* s_ch, const float* codebook, int group,
+                          const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N, int64_t K, int quant_mode,
+                          void* stream);
+
 /* Device-side failure flag of the current device: a kernel whose bounded wait ran out sets it (and returns instead of
  * hanging).  Returns the flag and, when clear != 0, resets it.  Synchronises the device. */
 int h3b_device_error(int clear);

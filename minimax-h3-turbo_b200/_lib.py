@@ -15,6 +15,7 @@ import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "libh3b.so"
 ABI_VERSION = 1
+NOALLOC_SCRATCH_BYTES = 16 << 20  # H3B_NOALLOC_SCRATCH_BYTES
 
 # enum h3b_status / h3b_dtype / h3b_quant_mode
 OK, ERR_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_DEVICE = 0, 1, 2, 3, 4
@@ -45,6 +46,8 @@ _SIGNATURES = {
                                 _i64, _i64, _i64, _int, _c_void_p], _int),
     "h3b_w4a8_linear": ([_c_void_p, _int, _i64, _i64, _i64, _int, _c_void_p, _i64, _c_void_p, _int, _i64, _c_void_p,
                          _c_void_p, _int, _int, _c_void_p, _c_void_p, _int, _i64, _i64, _int, _c_void_p, _sz, _c_void_p], _int),
+    "h3b_w4a8_gemm_noalloc": ([_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _int, _i64, _c_void_p,
+                               _c_void_p, _int, _c_void_p, _c_void_p, _int, _i64, _i64, _i64, _int, _c_void_p], _int),
     "h3b_device_error": ([_int], _int),
 }
 

@@ -1,6 +1,7 @@
 // libh3b.so: the C ABI declared in include/h3b.h, argument validation, error state, and the kernels (one translation
 // unit, so the device failure flag is a single symbol shared by every kernel).
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "h3b_common.cuh"
@@ -79,6 +80,34 @@ static int check_weight_args(const void* q4, int64_t N, int64_t K, int64_t ldq4,
   return H3B_OK;
 }
 
+}  // namespace h3b
+
+// ------------------------------------------------------------------------------------------------ allocation-free GEMM
+// h3b_w4a8_gemm_noalloc: the same decode + GEMM + epilogue as h3b_w4a8_gemm, for callers that cannot allocate device
+// memory (see include/h3b.h).  Its scratch -- the decoded int8 weight rows -- is this file-scope device array.  In host
+// code `g_noalloc_grid` names a host-side stand-in, not device memory, so its device address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) and only that address is handed to the kernels.
+static __device__ __align__(256) int8_t g_noalloc_grid[H3B_NOALLOC_SCRATCH_BYTES];
+
+namespace h3b {
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[64] = {};
+
+static int noalloc_scratch(void** addr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(H3B_ERR_UNSUPPORTED, "device ordinal >= 64");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_grid);
+    if (e != cudaSuccess || !p) return cuda_fail(e, "cudaGetSymbolAddress(allocation-free scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *addr = g_noalloc_addr[dev];
+  return H3B_OK;
+}
 }  // namespace h3b
 
 using namespace h3b;
@@ -207,6 +236,47 @@ int h3b_w4a8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld
   if (rc) return rc;
   return h3b_w4a8_gemm(qa, K, xs, M, q4, ldq4, s_rel, s_dtype, lds, s_ch, codebook, group, bias, out, out_dtype, ldo, N,
                        K, quant_mode, rest, ws_bytes - static_cast<size_t>(rest - ws), stream);
+}
+
+int h3b_w4a8_gemm_noalloc(const int8_t* qa, int64_t lda, const float* xs, int64_t M, const void* q4, int64_t ldq4,
+                          const void* s_rel, int s_dtype, int64_t lds, const float* s_ch, const float* codebook, int group,
+                          const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N, int64_t K, int quant_mode,
+                          void* stream) {
+  int rc = check_weight_args(q4, N, K, ldq4, s_rel, s_dtype, lds, codebook, group);
+  if (rc) return rc;
+  if (M < 0) return fail(H3B_ERR_ARG, "M must be >= 0");
+  if (out_dtype != H3B_BF16 && out_dtype != H3B_FP16 && out_dtype != H3B_FP32 && out_dtype != H3B_INT32)
+    return fail(H3B_ERR_ARG, "out dtype must be bf16, fp16, fp32 or int32");
+  if (quant_mode != H3B_QMODE_CK && quant_mode != H3B_QMODE_EAGER) return fail(H3B_ERR_ARG, "quant_mode must be 'ck' or 'eager'");
+  if (lda < K || lda % 16 || !aligned(qa, 16)) return fail(H3B_ERR_ARG, "activation codes must be 16-byte aligned with a row stride >= K, multiple of 16");
+  if (ldo < N) return fail(H3B_ERR_ARG, "ldo is smaller than N");
+  if (out_dtype != H3B_INT32 && (!s_ch || !xs)) return fail(H3B_ERR_ARG, "xs and s_ch must be given");
+  // slabs of `rows` weight rows (a multiple of 32, so every slab's output columns stay 16-byte aligned)
+  const int64_t rows = (static_cast<int64_t>(H3B_NOALLOC_SCRATCH_BYTES) / K) / 32 * 32;
+  if (rows < 32)
+    return fail(H3B_ERR_ARG, "K=" + std::to_string(K) + " exceeds the allocation-free limit: 32 decoded rows of K bytes must fit in the " +
+                                 std::to_string(H3B_NOALLOC_SCRATCH_BYTES) + "-byte scratch (K <= " +
+                                 std::to_string(H3B_NOALLOC_SCRATCH_BYTES / 32) + ")");
+  if (M == 0 || N == 0) return H3B_OK;
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int8_t* grid = static_cast<int8_t*>(scratch);
+  const size_t ssz = s_dtype == H3B_FP8_E4M3 ? 1 : (s_dtype == H3B_FP32 ? 4 : 2);
+  const size_t osz = (out_dtype == H3B_FP32 || out_dtype == H3B_INT32) ? 4 : 2;
+  for (int64_t n0 = 0; n0 < N; n0 += rows) {
+    const int64_t nr = N - n0 < rows ? N - n0 : rows;
+    rc = decode_launch(static_cast<const uint8_t*>(q4) + n0 * ldq4, nr, K, ldq4,
+                       static_cast<const char*>(s_rel) + static_cast<size_t>(n0 * lds) * ssz, s_dtype, lds, codebook,
+                       group, grid, K, st);
+    if (rc) return rc;
+    rc = gemm_launch(qa, lda, grid, K, xs, s_ch ? s_ch + n0 : nullptr,
+                     bias ? static_cast<const char*>(bias) + static_cast<size_t>(n0) * osz : nullptr,
+                     static_cast<char*>(out) + static_cast<size_t>(n0) * osz, out_dtype, ldo, M, nr, K, quant_mode, st);
+    if (rc) return rc;
+  }
+  return H3B_OK;
 }
 
 int h3b_device_error(int clear) {
