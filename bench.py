@@ -71,7 +71,7 @@ def peaks():
 
 # ------------------------------------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of SM clock and throttle reasons while the timed region runs."""
+    """nvidia-smi samples (every 50 ms) of SM clock and throttle reasons while the timed region runs."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -98,7 +98,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", self.sel], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                          "-lms", "50", "-i", self.sel], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                                          text=True)
         except OSError:
             self.proc = None

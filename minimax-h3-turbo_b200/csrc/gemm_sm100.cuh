@@ -123,11 +123,22 @@ __device__ __forceinline__ void epilogue_row32(const uint32_t (&r)[32], float xs
   }
 }
 
+// Tile order: "super-columns" of `gn` N tiles; inside one, N runs fastest and M next, so the CTAs working at the same
+// time share a weight block of gn x BN rows (sized by the host to stay resident in L2) and a slab of activation rows.
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int gn, int& mt, int& nt) {
+  const int group = tile / (gn * m_tiles);
+  const int first_n = group * gn;
+  const int width = min(gn, n_tiles - first_n);
+  const int local = tile - group * gn * m_tiles;
+  mt = local / width;
+  nt = first_n + (local - mt * width);
+}
+
 template <int BN, int OUT, bool BIAS, int QMODE>
 __global__ void __launch_bounds__(192, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const float* __restrict__ xs, const float* __restrict__ sch, const void* __restrict__ bias,
-                   void* __restrict__ out, int64_t ldo, int M, int N, int K) {
+                   void* __restrict__ out, int64_t ldo, int M, int N, int K, int gn) {
   using C = GemmCfg<BN>;
   extern __shared__ __align__(1024) unsigned char gemm_smem[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) & ~uintptr_t(1023));
@@ -178,7 +189,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       long long fills = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int mt = tile / n_tiles, nt = tile - mt * n_tiles;
+        int mt, nt;
+        tile_coords(tile, m_tiles, n_tiles, gn, mt, nt);
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
@@ -231,7 +243,8 @@ __global__ void __launch_bounds__(192, 1)
       const bool ok = mbar_wait(&tfull[buf], (it >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;  // tcgen05.ld below is warp-collective: leave together
       tc_fence_after();
-      const int mt = tile / n_tiles, nt = tile - mt * n_tiles;
+      int mt, nt;
+      tile_coords(tile, m_tiles, n_tiles, gn, mt, nt);
       const int row = mt * BM + quad * 32 + lane;
       const float xsr = (OUT != OUT_S32 && row < M) ? xs[row] : 0.f;
       char* orow = static_cast<char*>(out) + static_cast<size_t>(row) * static_cast<size_t>(ldo) * osz;
@@ -319,7 +332,11 @@ static int launch_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int sms = num_sms();
   const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, 192, C::SMEM, st>>>(ta, tb, xs, sch, bias, out, ldo, M, N, K);
+  // weight block per super-column <= ~24 MB of int8 rows, so it stays in L2 while every M tile passes over it
+  const int n_tiles = (N + BN - 1) / BN;
+  int gn = static_cast<int>((24ll << 20) / (static_cast<int64_t>(BN) * K));
+  gn = gn < 1 ? 1 : (gn > n_tiles ? n_tiles : gn);
+  kern<<<grid, 192, C::SMEM, st>>>(ta, tb, xs, sch, bias, out, ldo, M, N, K, gn);
   return check_launch("gemm_i8_kernel");
 }
 

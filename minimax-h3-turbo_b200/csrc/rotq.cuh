@@ -7,18 +7,30 @@
 //   q    = clamp(rint(dt(fp32(dt(y32)) / s)), -128, 127)                              :291-292
 //   with input_act="swiglu": x <- dt(dt(silu(gate)) * up) first                       _swiglu :376-379
 //
-// Layout.  A thread owns a 16-element chunk of TWO rows (a row pair), so every butterfly and every quantiser FMA is a
-// packed fp32x2 instruction with row A in .x and row B in .y.  Inside a ConvRot block of CR = 4^n elements, element
-// e has base-4 digits d0..d(n-1).  The chunk's 16 elements are digits d0, d1 (in registers); the CR/16 threads of a
-// block hold digits d2, d3.  Stage A transforms d0, d1 in registers; a swizzled shared-memory exchange regroups the
-// block so each thread holds all values of d2, d3 for a fixed (d0, d1); stage B transforms those.  The regular H4
-// butterfly is (H4 a)_i = S - 2 a_{3-i}, S = (a0 + a1) + (a2 + a3); the 1/sqrt(CR) normalisation (a power of two) is
-// folded into the last stage, which is exact.
+// Layout.  bf16/fp16: a thread owns TWO 16-element chunks ("lanes"), so every butterfly and quantiser FMA is a packed
+// fp32x2 instruction with lane 0 in .x and lane 1 in .y.  In split mode both lanes are the same row, K/2 elements apart
+// (K/32 threads per row; needs K to be a multiple of 32 x the threads of a ConvRot block so both lanes sit at the same
+// position of their blocks); otherwise the lanes are the same chunk of two rows (a row pair, K/16 threads).  fp32
+// activations: one chunk of one row per thread and the transform in fp64 -- exact for any fp32 input whose 256-block
+// spans under ~21 binades, i.e. the reference's correctly rounded fp64 rotation.  An exchanged value is 8 bytes
+// (float2 or double) either way.
+// Inside a ConvRot block of CR = 4^n elements, element e has base-4 digits d0..d(n-1).  The chunk's 16 elements are
+// digits d0, d1 (in registers); the CR/16 threads of a block hold digits d2, d3.  Stage A transforms d0, d1 in registers;
+// a padded shared-memory exchange regroups the block so each thread holds all values of d2, d3 for a fixed (d0, d1);
+// stage B transforms those.  The regular H4 butterfly is (H4 a)_i = S - 2 a_{3-i}, S = (a0 + a1) + (a2 + a3); the
+// 1/sqrt(CR) normalisation (a power of two) is folded into the last stage, which is exact.
 //
-// Division: s is constant per row, so q = dt(RN(b / s)) uses r = RN(1 / s) and one Markstein correction
-// (q0 = RN(b r), e = b - q0 s exactly, q1 = RN(q0 + e r)), which returns the correctly rounded quotient for every pair
-// of bf16 / fp16 operands (checked exhaustively over all significand pairs by tests/test_numerics.py); fp32
-// activations use the IEEE division directly.
+// Pipelining.  CTAs are persistent: each loops over row groups, and every thread loads its chunks of the NEXT group into
+// registers before transforming the current one, so HBM reads overlap the arithmetic and the CTA-wide row-max barrier.
+//
+// Division: s is constant per row.  bf16: RNbf16(RN(b r)) with r = RN(1/s) equals RNbf16(RN(b / s)) for every pair of
+// bf16 significands (checked exhaustively), so one multiply suffices.  fp16: r and one Markstein correction
+// (q0 = RN(b r), e = b - q0 s exactly, q1 = RN(q0 + e r)) -- the correctly rounded quotient for every pair of fp16
+// operands (checked exhaustively).  fp32 activations use the IEEE division.
+// Rounding the dt quotient to an integer uses the fp32 magic constant 1.5 * 2^23 (round half-to-even), after clamping
+// at 127 in the dt domain; the int8 code is the low byte of the sum's bit pattern.
+#include <type_traits>
+
 #include "h3b_common.cuh"
 
 namespace h3b {
@@ -27,18 +39,6 @@ enum { DT_BF16 = 0, DT_FP16 = 1, DT_FP32 = 2 };
 enum { MODE_CK = 0, MODE_EAGER = 1, MODE_ROTATE = 2 };
 
 // ------------------------------------------------------------------------------------------------ dtype helpers
-template <int DT>
-__device__ __forceinline__ float2 round_dt2(float2 v) {
-  if constexpr (DT == DT_BF16) {
-    const __nv_bfloat162 h = __float22bfloat162_rn(v);
-    return __bfloat1622float2(h);
-  } else if constexpr (DT == DT_FP16) {
-    const __half2 h = __float22half2_rn(v);
-    return __half22float2(h);
-  } else {
-    return v;
-  }
-}
 template <int DT>
 __device__ __forceinline__ float round_dt(float v) {
   if constexpr (DT == DT_BF16) return __bfloat162float(__float2bfloat16_rn(v));
@@ -49,37 +49,50 @@ template <int DT>
 __device__ __forceinline__ float tiny_dt() {
   return DT == DT_FP16 ? 6.103515625e-05f : 1.1754943508222875e-38f;  // torch.finfo(dt).tiny
 }
-
-// 16 consecutive activations of one row starting at element `off` -> fp32 (exact).  Row pointer 16-byte aligned.
+// bf16x2 / fp16x2 bit pattern -> the two values as fp32 (exact, integer ops for bf16)
 template <int DT>
-__device__ __forceinline__ void load16(const void* row, int64_t off, float (&v)[16]) {
-  if constexpr (DT == DT_FP32) {
-    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(row) + off);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 f = __ldg(p + i);
-      v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-    }
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if constexpr (DT == DT_BF16) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
   } else {
-    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(row) + off);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const uint4 u = __ldg(p + i);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if constexpr (DT == DT_BF16) {
-          v[8 * i + 2 * k] = __int_as_float(w[k] << 16);
-          v[8 * i + 2 * k + 1] = __int_as_float(w[k] & 0xFFFF0000u);
-        } else {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
-          v[8 * i + 2 * k] = f.x;
-          v[8 * i + 2 * k + 1] = f.y;
-        }
-      }
-    }
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
   }
 }
+// two fp32 values -> dt, packed (round to nearest even)
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float2 v) {
+  if constexpr (DT == DT_BF16) {
+    const __nv_bfloat162 h = __float22bfloat162_rn(v);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __half2 h = __float22half2_rn(v);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+// Packed clamp of the dt quotient before rounding.  bf16: |b / s| <= 127 (1 + 2^-8)^2 / (1 - 2^-24) < 128.5, so only
+// the top needs a clamp (rint(127.5) = 128 -> 127); fp16 also clamps at -128 (an overflowed fp16 rotation can reach it).
+template <int DT>
+__device__ __forceinline__ uint32_t clamp_q2(uint32_t w) {
+  if constexpr (DT == DT_BF16) {
+    const __nv_bfloat162 r = __hmin2(*reinterpret_cast<const __nv_bfloat162*>(&w), __float2bfloat162_rn(127.0f));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  } else {
+    const __half2 r = __hmax2(__hmin2(*reinterpret_cast<const __half2*>(&w), __float2half2_rn(127.0f)), __float2half2_rn(-128.0f));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+}
+// Round two fp32 values to the nearest bf16 (ties to even), returned as fp32, on the FMA pipe: Veltkamp splitting with
+// C = 2^16 + 1 (g = v C, d = v - g, h = g + d; each step rounded once, never contracted).  Equal to round-to-nearest-even
+// for every fp32 significand whenever all intermediates are normal and finite, i.e. for |v| in [2^-125, 2^111) (checked
+// exhaustively by tests/test_numerics.py); callers use it only below 2^100 -- values under 2^-110 quantise to code 0
+// whatever their last bf16 bit.
+__device__ __forceinline__ float2 rne_bf16_fma(float2 v) {
+  const float2 g = __fmul2_rn(v, make_float2(65537.0f, 65537.0f));
+  const float2 d = __ffma2_rn(g, make_float2(-1.0f, -1.0f), v);
+  return __fadd2_rn(g, d);
+}
+constexpr float VELTKAMP_MAX = 1.2676506002282294e30f;  // 2^100
+constexpr float RINT_MAGIC = 12582912.0f;  // 1.5 * 2^23: x + M rounds x to an integer (half-to-even) for |x| < 2^22
 
 // silu(gate) * up in dt, as torch computes it: x / (1 + exp(-x)) in fp32, rounded to dt; the product of the two dt
 // values in fp32, rounded to dt.
@@ -89,280 +102,422 @@ __device__ __forceinline__ float swiglu1(float g, float u) {
   return round_dt<DT>(sl * u);
 }
 
-template <int DT, bool SWIGLU>
-__device__ __forceinline__ void load_chunk(const void* x, int64_t ldx, int64_t row, bool valid, int64_t col, int K,
-                                           float (&v)[16]) {
-  if (!valid) {
+// ------------------------------------------------------------------------------------------------ lanes
+// A thread's inputs: L lanes (2 for bf16/fp16, 1 for fp32) of 16 elements; each lane is (row offset, column offset)
+// from the thread's (row0, col): split mode (0, l K/2), pair mode (l, 0).
+template <int DT, bool SW>
+struct Raw {
+  static constexpr int L = DT == DT_FP32 ? 1 : 2;
+  static constexpr int ESZ = DT == DT_FP32 ? 4 : 2;      // bytes per element
+  static constexpr int V16 = ESZ;                        // uint4 per 16 elements (32 or 64 bytes)
+  uint4 u[L * V16 * (SW ? 2 : 1)];
+};
+
+template <int DT, bool SW, bool SPLIT>
+__device__ __forceinline__ void load_raw(Raw<DT, SW>& raw, const void* x, int64_t ldx, int64_t row0, int M, int64_t col,
+                                         int K) {
+  using RW = Raw<DT, SW>;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = 0.f;
-    return;
+  for (int l = 0; l < RW::L; ++l) {
+    const int64_t row = row0 + (SPLIT ? 0 : l);
+    const int64_t c0 = col + (SPLIT ? l * (K / 2) : 0);
+    const bool valid = row < M;
+    const char* base = static_cast<const char*>(x) + static_cast<size_t>(valid ? row : 0) * static_cast<size_t>(ldx) * RW::ESZ;
+#pragma unroll
+    for (int h = 0; h < (SW ? 2 : 1); ++h) {
+      const uint4* ptr = reinterpret_cast<const uint4*>(base + static_cast<size_t>(c0 + h * K) * RW::ESZ);
+#pragma unroll
+      for (int i = 0; i < RW::V16; ++i)
+        raw.u[(l * (SW ? 2 : 1) + h) * RW::V16 + i] = valid ? __ldg(ptr + i) : make_uint4(0, 0, 0, 0);
+    }
   }
-  const size_t esz = DT == DT_FP32 ? 4 : 2;
-  const char* r = static_cast<const char*>(x) + static_cast<size_t>(row) * static_cast<size_t>(ldx) * esz;
-  load16<DT>(r, col, v);
-  if constexpr (SWIGLU) {
-    float u[16];
-    load16<DT>(r, col + K, u);
+}
+
+// lane l of `raw` -> 16 fp32 values (SwiGLU applied)
+template <int DT, bool SW>
+__device__ __forceinline__ void lane_f32(const Raw<DT, SW>& raw, int l, float (&v)[16]) {
+  using RW = Raw<DT, SW>;
+  float u[SW ? 16 : 1];
+#pragma unroll
+  for (int h = 0; h < (SW ? 2 : 1); ++h) {
+    float* dst = h == 0 ? v : u;
+    const uint4* src = raw.u + (l * (SW ? 2 : 1) + h) * RW::V16;
+    if constexpr (DT == DT_FP32) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        dst[4 * i] = __uint_as_float(src[i].x); dst[4 * i + 1] = __uint_as_float(src[i].y);
+        dst[4 * i + 2] = __uint_as_float(src[i].z); dst[4 * i + 3] = __uint_as_float(src[i].w);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint32_t w[4] = {src[i].x, src[i].y, src[i].z, src[i].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = unpack2<DT>(w[k]);
+          dst[8 * i + 2 * k] = f.x;
+          dst[8 * i + 2 * k + 1] = f.y;
+        }
+      }
+    }
+  }
+  if constexpr (SW) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = swiglu1<DT>(v[i], u[i]);
   }
 }
 
 // ------------------------------------------------------------------------------------------------ butterflies
-__device__ __forceinline__ void h4x2(float2& a0, float2& a1, float2& a2, float2& a3) {
-  const float2 s = __fadd2_rn(__fadd2_rn(a0, a1), __fadd2_rn(a2, a3));
-  const float2 m2 = make_float2(-2.f, -2.f);
-  const float2 y0 = __ffma2_rn(m2, a3, s), y1 = __ffma2_rn(m2, a2, s);
-  const float2 y2 = __ffma2_rn(m2, a1, s), y3 = __ffma2_rn(m2, a0, s);
-  a0 = y0; a1 = y1; a2 = y2; a3 = y3;
-}
-// Same butterfly, result scaled by the power of two `sc` (exact).
-__device__ __forceinline__ void h4x2s(float2& a0, float2& a1, float2& a2, float2& a3, float sc) {
-  const float2 s = __fmul2_rn(__fadd2_rn(__fadd2_rn(a0, a1), __fadd2_rn(a2, a3)), make_float2(sc, sc));
+// float2: two rows in lockstep (packed fp32x2); double: one fp32-input row in fp64.
+__device__ __forceinline__ void h4(float2& a0, float2& a1, float2& a2, float2& a3, float sc) {
+  float2 s = __fadd2_rn(__fadd2_rn(a0, a1), __fadd2_rn(a2, a3));
+  if (sc != 1.0f) s = __fmul2_rn(s, make_float2(sc, sc));
   const float2 m2 = make_float2(-2.f * sc, -2.f * sc);
   const float2 y0 = __ffma2_rn(m2, a3, s), y1 = __ffma2_rn(m2, a2, s);
   const float2 y2 = __ffma2_rn(m2, a1, s), y3 = __ffma2_rn(m2, a0, s);
   a0 = y0; a1 = y1; a2 = y2; a3 = y3;
 }
+__device__ __forceinline__ void h4(double& a0, double& a1, double& a2, double& a3, float sc) {
+  const double s = ((a0 + a1) + (a2 + a3)) * static_cast<double>(sc);
+  const double m2 = -2.0 * static_cast<double>(sc);
+  const double y0 = fma(m2, a3, s), y1 = fma(m2, a2, s), y2 = fma(m2, a1, s), y3 = fma(m2, a0, s);
+  a0 = y0; a1 = y1; a2 = y2; a3 = y3;
+}
+
+// ------------------------------------------------------------------------------------------------ exchange layout
+// Per ConvRot block of G threads: owner t's 16 values (8 bytes each) in row t of a [G][18] array of 8-byte slots
+// (144-byte rows: 16-byte aligned, and consecutive rows shift by one 16-byte bank group, so both the owners' 16-byte
+// stores and the readers' 8-byte loads are conflict-free).  Blocks are g x 144 + 64 bytes apart (a half-bank shift).
+constexpr int XROW = 18;                       // 8-byte slots per owner row
+__host__ __device__ constexpr int xgrp(int g) { return g * XROW + 8; }  // 8-byte slots per ConvRot block of g threads
+// Code regroup: 16 chunks of 16 x (A, B) byte pairs, chunk stride 48 bytes (conflict-free 16-byte reads).
+constexpr int CSTRIDE = 48;
 
 // ------------------------------------------------------------------------------------------------ the kernel
-// blockDim.x = tpr * pairs; tpr = K / 16 threads per row pair.  Row pair p of the CTA: rows 2(blockIdx.x*pairs+p)+{0,1}.
-template <int DT, int CR, int MODE, bool SWIGLU>
-__global__ void __launch_bounds__(1024) rotq_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int tpr,
-                                                     int pairs, int8_t* __restrict__ q, int64_t ldq,
-                                                     float* __restrict__ xs_out, void* __restrict__ y_out,
-                                                     int y_dtype, int64_t ldy) {
+// blockDim.x = tpr * groups_per_cta; tpr = K / 32 (split) or K / 16 threads per row group; a row group is 1 row (split,
+// fp32) or 2 rows (pair).  Persistent: group g = blockIdx.x * groups_per_cta + p, then += gridDim.x * groups_per_cta.
+template <int DT, int CR, int MODE, bool SW, bool SPLIT>
+__global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __restrict__ x, int64_t ldx, int M, int K,
+                                                                   int tpr, int pairs, int8_t* __restrict__ q, int64_t ldq,
+                                                                   float* __restrict__ xs_out, void* __restrict__ y_out,
+                                                                   int y_dtype, int64_t ldy) {
   constexpr int G = CR >= 256 ? 16 : (CR == 64 ? 4 : 1);  // threads per ConvRot block
   constexpr float SCALE = CR == 256 ? 0.0625f : CR == 64 ? 0.125f : CR == 16 ? 0.25f : 0.5f;
+  constexpr int L = DT == DT_FP32 ? 1 : 2;                // lanes per thread
+  constexpr int RG = (SPLIT || L == 1) ? 1 : 2;           // rows per row group
+  using T = typename std::conditional<DT == DT_FP32, double, float2>::type;
   extern __shared__ __align__(16) unsigned char rotq_smem[];
-  unsigned int* rowmax = reinterpret_cast<unsigned int*>(rotq_smem);  // [2 * pairs]
-  float2* xbuf = reinterpret_cast<float2*>(rotq_smem + 16 * ((2 * pairs * 4 + 15) / 16));  // [blockDim][16]
+  unsigned int* rowmax = reinterpret_cast<unsigned int*>(rotq_smem);  // [3 slots][pairs * RG]
+  T* xbuf = reinterpret_cast<T*>(rotq_smem + 16 * ((3 * pairs * RG * 4 + 15) / 16));
 
   const int tid = threadIdx.x;
-  const int p = tid / tpr, tr = tid - p * tpr;  // pair in CTA, thread in row
-  const int64_t rowA = 2ll * (static_cast<int64_t>(blockIdx.x) * pairs + p);
-  const bool vA = rowA < M, vB = rowA + 1 < M;
-  const int64_t col = 16ll * tr;
+  const int p = tid / tpr, tr = tid - p * tpr;
+  const int t = tr % G;                                  // thread within the ConvRot block
+  const int64_t col = 16ll * tr;                         // lane 0's first element
+  const int64_t blk0 = static_cast<int64_t>(tr - t) * 16;  // first element of lane 0's ConvRot block
+  T* gbuf = xbuf + static_cast<size_t>((tid - t) / G) * xgrp(G);
+  const int64_t ngroups = (static_cast<int64_t>(M) + RG - 1) / RG;
+  const int64_t gstep = static_cast<int64_t>(gridDim.x) * pairs;
+  const int64_t lane_col = SPLIT ? K / 2 : 0;            // lane 1's column offset
 
-  if (tid < 2 * pairs) rowmax[tid] = 0u;
-
-  float2 v[16];
-  {
-    float a[16], b[16];
-    load_chunk<DT, SWIGLU>(x, ldx, rowA, vA, col, K, a);
-    load_chunk<DT, SWIGLU>(x, ldx, rowA + 1, vB, col, K, b);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = make_float2(a[i], b[i]);
-  }
-
-  // ---- stage A: digits d0 (register bits 0-1) and d1 (register bits 2-3)
-  if constexpr (CR == 4) {
-#pragma unroll
-    for (int g = 0; g < 4; ++g) h4x2s(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3], SCALE);
-  } else {
-#pragma unroll
-    for (int g = 0; g < 4; ++g) h4x2(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-#pragma unroll
-    for (int d = 0; d < 4; ++d) {
-      if constexpr (CR == 16) h4x2s(v[d], v[d + 4], v[d + 8], v[d + 12], SCALE);
-      else h4x2(v[d], v[d + 4], v[d + 8], v[d + 12]);
-    }
-  }
-
-  // ---- exchange + stage B (digits d2, d3 across the G threads of the block)
-  const int t = tr % G;                       // thread within the ConvRot block
-  float2* gbuf = xbuf + static_cast<size_t>(tid - t) * 16;  // this block's G x 16 float2
-  if constexpr (G > 1) {
-    // write own 16 values as eight 16-byte chunks, chunk index XOR-swizzled by the owner so stores are conflict-free
-    float4* wr = reinterpret_cast<float4*>(gbuf + t * 16);
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      wr[i ^ (t & 7)] = make_float4(v[2 * i].x, v[2 * i].y, v[2 * i + 1].x, v[2 * i + 1].y);
-    __syncwarp();
-    if constexpr (G == 16) {
-      // v[j] <- owner j's element r = t   (register j = d2 + 4 d3)
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float2* src = gbuf + j * 16;
-        v[j] = src[2 * ((t >> 1) ^ (j & 7)) + (t & 1)];
-      }
-      __syncwarp();
-#pragma unroll
-      for (int g = 0; g < 4; ++g) h4x2(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-#pragma unroll
-      for (int d = 0; d < 4; ++d) h4x2s(v[d], v[d + 4], v[d + 8], v[d + 12], SCALE);
-    } else {
-      // G == 4: v[4 j + d0] <- owner j's elements r = 4t + d0  (register 4j + d0; digit d2 = j)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float4* src = reinterpret_cast<const float4*>(gbuf + j * 16);
-        const float4 c0 = src[(2 * t) ^ (j & 7)], c1 = src[(2 * t + 1) ^ (j & 7)];
-        v[4 * j + 0] = make_float2(c0.x, c0.y);
-        v[4 * j + 1] = make_float2(c0.z, c0.w);
-        v[4 * j + 2] = make_float2(c1.x, c1.y);
-        v[4 * j + 3] = make_float2(c1.z, c1.w);
-      }
-      __syncwarp();
-#pragma unroll
-      for (int d = 0; d < 4; ++d) h4x2s(v[d], v[d + 4], v[d + 8], v[d + 12], SCALE);
-    }
-  }
-  // element index (within the row) of register i
-  const int64_t blk0 = static_cast<int64_t>(tr - t) * 16;  // first element of this ConvRot block
-  auto elem = [&](int i) -> int64_t {
+  auto elem = [&](int i) -> int64_t {  // lane-0 element (within the row) of register i after the transform
     if constexpr (G == 16) return blk0 + t + 16 * i;
     else if constexpr (G == 4) return blk0 + 16 * (i >> 2) + 4 * t + (i & 3);
     else return col + i;
   };
 
-  if constexpr (MODE == MODE_ROTATE) {
-    const size_t ysz = y_dtype == 2 ? 4 : 2;
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      if (!(rr == 0 ? vA : vB)) continue;
-      char* yr = static_cast<char*>(y_out) + static_cast<size_t>(rowA + rr) * static_cast<size_t>(ldy) * ysz;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float val = rr == 0 ? v[i].x : v[i].y;
-        const int64_t e = elem(i);
-        if (y_dtype == 0) reinterpret_cast<__nv_bfloat16*>(yr)[e] = __float2bfloat16_rn(val);
-        else if (y_dtype == 1) reinterpret_cast<__half*>(yr)[e] = __float2half_rn(val);
-        else reinterpret_cast<float*>(yr)[e] = val;
-      }
-    }
-    return;
-  } else {
-    // ---- dt rounding and the row absmax
-    float2 b[16];
-    float mA = 0.f, mB = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      b[i] = round_dt2<DT>(v[i]);
-      const float2 src = MODE == MODE_CK ? v[i] : b[i];
-      mA = fmaxf(mA, fabsf(src.x));
-      mB = fmaxf(mB, fabsf(src.y));
-    }
-    __syncthreads();  // rowmax initialised
-    if ((tpr & 31) == 0) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        mA = fmaxf(mA, __shfl_xor_sync(0xffffffffu, mA, o));
-        mB = fmaxf(mB, __shfl_xor_sync(0xffffffffu, mB, o));
-      }
-      if ((tid & 31) == 0) {
-        atomicMax(&rowmax[2 * p], __float_as_uint(mA));
-        atomicMax(&rowmax[2 * p + 1], __float_as_uint(mB));
-      }
-    } else {
-      atomicMax(&rowmax[2 * p], __float_as_uint(mA));
-      atomicMax(&rowmax[2 * p + 1], __float_as_uint(mB));
-    }
-    __syncthreads();
-    const float amaxA = __uint_as_float(rowmax[2 * p]), amaxB = __uint_as_float(rowmax[2 * p + 1]);
-    const float xsA = fmaxf(__fdiv_rn(amaxA, 127.0f), 1e-30f), xsB = fmaxf(__fdiv_rn(amaxB, 127.0f), 1e-30f);
-    float sA = round_dt<DT>(xsA), sB = round_dt<DT>(xsB);
-    if (sA == 0.f) sA = tiny_dt<DT>();
-    if (sB == 0.f) sB = tiny_dt<DT>();
-    if (tr == 0) {
-      if (vA) xs_out[rowA] = xsA;
-      if (vB) xs_out[rowA + 1] = xsB;
-    }
+  for (int s = tid; s < 3 * pairs * RG; s += blockDim.x) rowmax[s] = 0u;
+  __syncthreads();
 
-    // ---- quantise: c = sat_s8(rint(dt(RN(b / s))))
-    uint32_t c[16];
+  int64_t g = static_cast<int64_t>(blockIdx.x) * pairs + p;
+  Raw<DT, SW> raw;
+  load_raw<DT, SW, SPLIT>(raw, x, ldx, g * RG, M, col, K);
+  int slot = 0;
+  for (int64_t gbase = static_cast<int64_t>(blockIdx.x) * pairs; gbase < ngroups; gbase += gstep, g += gstep) {
+    const int64_t row0 = g * RG;
+    // ---- this group's values, then prefetch the next group's raw inputs into the same registers
+    T v[16];
     if constexpr (DT == DT_FP32) {
+      float f[16];
+      lane_f32<DT, SW>(raw, 0, f);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float qa = __fdiv_rn(b[i].x, sA), qb = __fdiv_rn(b[i].y, sB);
-        int ia, ib;
-        asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(ia) : "f"(qa));
-        asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(ib) : "f"(qb));
-        c[i] = (static_cast<uint32_t>(ia) & 0xFFu) | ((static_cast<uint32_t>(ib) & 0xFFu) << 8);
+      for (int i = 0; i < 16; ++i) v[i] = static_cast<double>(f[i]);
+    } else if constexpr (!SW) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {  // words of lane 0 (raw.u[0..1]) and lane 1 (raw.u[2..3]), 2 elements per word
+        const uint32_t wa[4] = {raw.u[i].x, raw.u[i].y, raw.u[i].z, raw.u[i].w};
+        const uint32_t wb[4] = {raw.u[2 + i].x, raw.u[2 + i].y, raw.u[2 + i].z, raw.u[2 + i].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 a = unpack2<DT>(wa[k]), b = unpack2<DT>(wb[k]);
+          v[8 * i + 2 * k] = make_float2(a.x, b.x);
+          v[8 * i + 2 * k + 1] = make_float2(a.y, b.y);
+        }
       }
     } else {
-      const float2 S2 = make_float2(sA, sB), nS2 = make_float2(-sA, -sB);
-      const float2 R2 = make_float2(__frcp_rn(sA), __frcp_rn(sB));
+      float f[16];
+      lane_f32<DT, SW>(raw, 0, f);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float2 q0 = __fmul2_rn(b[i], R2);
-        const float2 e = __ffma2_rn(q0, nS2, b[i]);
-        const float2 q1 = round_dt2<DT>(__ffma2_rn(e, R2, q0));
-        int ia, ib;
-        asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(ia) : "f"(q1.x));
-        asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(ib) : "f"(q1.y));
-        c[i] = (static_cast<uint32_t>(ia) & 0xFFu) | ((static_cast<uint32_t>(ib) & 0xFFu) << 8);
+      for (int i = 0; i < 16; ++i) v[i].x = f[i];
+      lane_f32<DT, SW>(raw, 1, f);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i].y = f[i];
+    }
+    if (gbase + gstep < ngroups) load_raw<DT, SW, SPLIT>(raw, x, ldx, (g + gstep) * RG, M, col, K);
+
+    // ---- stage A: digits d0 (register bits 0-1) and d1 (register bits 2-3)
+    if constexpr (CR == 4) {
+#pragma unroll
+      for (int a = 0; a < 4; ++a) h4(v[4 * a], v[4 * a + 1], v[4 * a + 2], v[4 * a + 3], SCALE);
+    } else {
+#pragma unroll
+      for (int a = 0; a < 4; ++a) h4(v[4 * a], v[4 * a + 1], v[4 * a + 2], v[4 * a + 3], 1.0f);
+#pragma unroll
+      for (int d = 0; d < 4; ++d) h4(v[d], v[d + 4], v[d + 8], v[d + 12], CR == 16 ? SCALE : 1.0f);
+    }
+    // ---- exchange + stage B (digits d2, d3 across the G threads of the block)
+    if constexpr (G > 1) {
+      float4* wr = reinterpret_cast<float4*>(gbuf + t * XROW);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if constexpr (DT == DT_FP32) {
+          wr[i] = make_float4(__int_as_float(__double2loint(v[2 * i])), __int_as_float(__double2hiint(v[2 * i])),
+                              __int_as_float(__double2loint(v[2 * i + 1])), __int_as_float(__double2hiint(v[2 * i + 1])));
+        } else {
+          wr[i] = make_float4(v[2 * i].x, v[2 * i].y, v[2 * i + 1].x, v[2 * i + 1].y);
+        }
       }
-      (void)S2;
+      __syncwarp();
+      if constexpr (G == 16) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = gbuf[j * XROW + t];  // owner j's element r = t (register j = d2 + 4 d3)
+        __syncwarp();
+#pragma unroll
+        for (int a = 0; a < 4; ++a) h4(v[4 * a], v[4 * a + 1], v[4 * a + 2], v[4 * a + 3], 1.0f);
+#pragma unroll
+        for (int d = 0; d < 4; ++d) h4(v[d], v[d + 4], v[d + 8], v[d + 12], SCALE);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+          for (int d = 0; d < 4; ++d) v[4 * j + d] = gbuf[j * XROW + 4 * t + d];  // owner j's r = 4t + d0
+        }
+        __syncwarp();
+#pragma unroll
+        for (int d = 0; d < 4; ++d) h4(v[d], v[d + 4], v[d + 8], v[d + 12], SCALE);
+      }
     }
 
-    // ---- store the codes of both rows (16 contiguous bytes each)
-    uint32_t wA[4], wB[4];
-    if constexpr (G == 1) {
+    if constexpr (MODE == MODE_ROTATE) {
+      const size_t ysz = y_dtype == H3B_FP32 ? 4 : 2;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        wA[w] = __byte_perm(__byte_perm(c[4 * w], c[4 * w + 1], 0x0040), __byte_perm(c[4 * w + 2], c[4 * w + 3], 0x0040), 0x5410);
-        wB[w] = __byte_perm(__byte_perm(c[4 * w], c[4 * w + 1], 0x0051), __byte_perm(c[4 * w + 2], c[4 * w + 3], 0x0051), 0x5410);
+      for (int l = 0; l < L; ++l) {
+        const int64_t row = row0 + (SPLIT ? 0 : l);
+        if (row >= M) continue;
+        char* yr = static_cast<char*>(y_out) + static_cast<size_t>(row) * static_cast<size_t>(ldy) * ysz;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float val;
+          if constexpr (DT == DT_FP32) val = static_cast<float>(v[i]);
+          else val = l == 0 ? v[i].x : v[i].y;
+          const int64_t e = elem(i) + l * lane_col;
+          if (y_dtype == H3B_BF16) reinterpret_cast<__nv_bfloat16*>(yr)[e] = __float2bfloat16_rn(val);
+          else if (y_dtype == H3B_FP16) reinterpret_cast<__half*>(yr)[e] = __float2half_rn(val);
+          else reinterpret_cast<float*>(yr)[e] = val;
+        }
       }
+      continue;
     } else {
-      // regroup through shared memory: interleaved (A, B) byte pairs at each element of this block
-      uint16_t* cb = reinterpret_cast<uint16_t*>(gbuf);
+      // ---- dt rounding (b, kept as fp32 values) and the local absmax
+      float2 b2[16];       // bf16/fp16: dt(y) of (lane 0, lane 1)
+      uint32_t bw[16];     // fp32 activations: the fp32 value of the single lane
+      float mA = 0.f, mB = 0.f;
+      if constexpr (DT == DT_FP32) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) cb[elem(i) - blk0] = static_cast<uint16_t>(c[i]);
-      __syncwarp();
-      const uint4* rd = reinterpret_cast<const uint4*>(cb + 16 * t);
-      const uint4 u0 = rd[0], u1 = rd[1];
-      const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        for (int i = 0; i < 16; ++i) {
+          const float y = static_cast<float>(v[i]);
+          bw[i] = __float_as_uint(y);
+          mA = fmaxf(mA, fabsf(y));
+        }
+      } else if constexpr (DT == DT_BF16 && MODE == MODE_CK) {
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        wA[w] = __byte_perm(w8[2 * w], w8[2 * w + 1], 0x6420);
-        wB[w] = __byte_perm(w8[2 * w], w8[2 * w + 1], 0x7531);
+        for (int i = 0; i < 16; ++i) {
+          mA = fmaxf(mA, fabsf(v[i].x));
+          mB = fmaxf(mB, fabsf(v[i].y));
+        }
+        if (fmaxf(mA, mB) < VELTKAMP_MAX) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) b2[i] = rne_bf16_fma(v[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) b2[i] = unpack2<DT>(pack2<DT>(v[i]));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          b2[i] = unpack2<DT>(pack2<DT>(v[i]));
+          const float2 src = MODE == MODE_CK ? v[i] : b2[i];
+          mA = fmaxf(mA, fabsf(src.x));
+          mB = fmaxf(mB, fabsf(src.y));
+        }
+      }
+      if constexpr (RG == 1 && L == 2) mA = fmaxf(mA, mB);  // split: both lanes are the same row
+      unsigned int* rm = rowmax + slot * pairs * RG + p * RG;
+      if ((tpr & 31) == 0) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          mA = fmaxf(mA, __shfl_xor_sync(0xffffffffu, mA, o));
+          if (RG == 2) mB = fmaxf(mB, __shfl_xor_sync(0xffffffffu, mB, o));
+        }
+        if ((tid & 31) == 0) {
+          atomicMax(&rm[0], __float_as_uint(mA));
+          if (RG == 2) atomicMax(&rm[RG - 1], __float_as_uint(mB));
+        }
+      } else {
+        atomicMax(&rm[0], __float_as_uint(mA));
+        if (RG == 2) atomicMax(&rm[RG - 1], __float_as_uint(mB));
+      }
+      __syncthreads();
+      // slot (slot + 2) % 3 was last read before the previous barrier and is next written after the next one
+      {
+        const int clr = slot == 0 ? 2 : slot - 1;
+        for (int s2 = tid; s2 < pairs * RG; s2 += blockDim.x) rowmax[clr * pairs * RG + s2] = 0u;
+      }
+      const float amaxA = __uint_as_float(rm[0]), amaxB = __uint_as_float(rm[RG - 1]);
+      slot = slot == 2 ? 0 : slot + 1;
+      const float xsA = fmaxf(__fdiv_rn(amaxA, 127.0f), 1e-30f);
+      const float xsB = RG == 2 ? fmaxf(__fdiv_rn(amaxB, 127.0f), 1e-30f) : xsA;
+      float sA = round_dt<DT>(xsA);
+      if (sA == 0.f) sA = tiny_dt<DT>();
+      float sB = sA;
+      if (RG == 2) {
+        sB = round_dt<DT>(xsB);
+        if (sB == 0.f) sB = tiny_dt<DT>();
+      }
+      if (tr == 0) {
+        if (row0 < M) xs_out[row0] = xsA;
+        if (RG == 2 && row0 + 1 < M) xs_out[row0 + 1] = xsB;
+      }
+
+      // ---- quantise: code = sat_s8(rint(dt(RN(b / s)))); cpair(i) = lane 0 code | lane 1 code << 8
+      unsigned char* cbuf = reinterpret_cast<unsigned char*>(gbuf);  // G > 1: regroup area (the exchange is done)
+      // (lane 0, lane 1) byte pairs by element e of the block; the 16 elements of chunk c at c * CSTRIDE bytes.
+      // G = 16: register i is element t + 16 i (chunk i, slot t); G = 4: 16 (i >> 2) + 4 t + (i & 3).
+      unsigned char* cb_t = cbuf + (G == 16 ? 2 * t : 8 * t);
+      uint32_t wA[4] = {0, 0, 0, 0}, wB[4] = {0, 0, 0, 0};
+      auto put = [&](int i, uint32_t cpair) {
+        if constexpr (G == 1) {  // own 16 contiguous elements: pack in registers
+          wA[i >> 2] |= (cpair & 0xFFu) << (8 * (i & 3));
+          wB[i >> 2] |= ((cpair >> 8) & 0xFFu) << (8 * (i & 3));
+        } else if constexpr (G == 16) {
+          *reinterpret_cast<uint16_t*>(cb_t + i * CSTRIDE) = static_cast<uint16_t>(cpair);
+        } else {
+          *reinterpret_cast<uint16_t*>(cb_t + (i >> 2) * CSTRIDE + 2 * (i & 3)) = static_cast<uint16_t>(cpair);
+        }
+      };
+      if constexpr (DT == DT_FP32) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float qv = fminf(__fdiv_rn(__uint_as_float(bw[i]), sA), 127.0f);
+          qv = fmaxf(qv, -128.0f);
+          put(i, __float_as_uint(qv + RINT_MAGIC) & 0xFFu);
+        }
+      } else {
+        const float2 nS2 = make_float2(-sA, -sB);
+        const float rA = __frcp_rn(sA);
+        const float2 R2 = make_float2(rA, RG == 2 ? __frcp_rn(sB) : rA);
+        const float2 MG = make_float2(RINT_MAGIC, RINT_MAGIC);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 b = b2[i];
+          const float2 q0 = __fmul2_rn(b, R2);
+          float2 qd;
+          if constexpr (DT == DT_BF16) {
+            // RNbf16(q0) is RNbf16(b / s); clamp at 127 first (same codes: every quotient > 127 ends at 127)
+            qd = rne_bf16_fma(make_float2(fminf(q0.x, 127.0f), fminf(q0.y, 127.0f)));
+          } else {
+            const float2 e = __ffma2_rn(q0, nS2, b);
+            qd = unpack2<DT>(clamp_q2<DT>(pack2<DT>(__ffma2_rn(e, R2, q0))));  // dt(RN(b / s)), clamped
+          }
+          const float2 rr = __fadd2_rn(qd, MG);  // rint, half-to-even
+          put(i, __byte_perm(__float_as_uint(rr.x), __float_as_uint(rr.y), 0x0040));
+        }
+      }
+      if constexpr (G > 1) {
+        __syncwarp();
+        const uint4* rd = reinterpret_cast<const uint4*>(cbuf + t * CSTRIDE);
+        const uint4 u0 = rd[0], u1 = rd[1];
+        const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          wA[w] = __byte_perm(w8[2 * w], w8[2 * w + 1], 0x6420);
+          wB[w] = __byte_perm(w8[2 * w], w8[2 * w + 1], 0x7531);
+        }
+        __syncwarp();
+      }
+      // ---- store: lane 0 -> (row0, col), lane 1 -> split: (row0, col + K/2), pair: (row0 + 1, col)
+      if (row0 < M) *reinterpret_cast<uint4*>(q + row0 * ldq + col) = make_uint4(wA[0], wA[1], wA[2], wA[3]);
+      if constexpr (L == 2) {
+        const int64_t row1 = row0 + (SPLIT ? 0 : 1);
+        if (row1 < M) *reinterpret_cast<uint4*>(q + row1 * ldq + col + lane_col) = make_uint4(wB[0], wB[1], wB[2], wB[3]);
       }
     }
-    if (vA) *reinterpret_cast<uint4*>(q + rowA * ldq + col) = make_uint4(wA[0], wA[1], wA[2], wA[3]);
-    if (vB) *reinterpret_cast<uint4*>(q + (rowA + 1) * ldq + col) = make_uint4(wB[0], wB[1], wB[2], wB[3]);
   }
 }
 
 // ------------------------------------------------------------------------------------------------ launcher
-struct RotqLaunch {
-  int tpr, pairs, threads, blocks;
-  size_t smem;
-};
-
-static RotqLaunch plan(int64_t M, int64_t K) {
-  RotqLaunch L;
-  L.tpr = static_cast<int>(K / 16);
-  L.pairs = L.tpr >= 256 ? 1 : (256 + L.tpr - 1) / L.tpr;
-  while (L.pairs > 1 && L.pairs * L.tpr > 1024) --L.pairs;
-  L.threads = L.pairs * L.tpr;
-  const int64_t row_pairs = (M + 1) / 2;
-  L.blocks = static_cast<int>((row_pairs + L.pairs - 1) / L.pairs);
-  L.smem = 16 * ((2 * L.pairs * 4 + 15) / 16) + static_cast<size_t>(L.threads) * 16 * sizeof(float2);
-  return L;
-}
-
-template <int DT, int CR, int MODE, bool SW>
+template <int DT, int CR, int MODE, bool SW, bool SPLIT>
 static int launch_t(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, int64_t ldq, float* xs, void* y,
                     int ydt, int64_t ldy, cudaStream_t st) {
-  const RotqLaunch L = plan(M, K);
-  auto kern = rotq_kernel<DT, CR, MODE, SW>;
-  if (L.smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.smem));
+  constexpr int L = DT == DT_FP32 ? 1 : 2;
+  constexpr int RG = (SPLIT || L == 1) ? 1 : 2;
+  constexpr int G = CR >= 256 ? 16 : (CR == 64 ? 4 : 1);
+  constexpr int MAXT = SPLIT ? 512 : 1024;
+  using T = typename std::conditional<DT == DT_FP32, double, float2>::type;
+  const int tpr = static_cast<int>(SPLIT ? K / 32 : K / 16);
+  int pairs = tpr >= 256 ? 1 : (256 + tpr - 1) / tpr;
+  while (pairs > 1 && pairs * tpr > MAXT) --pairs;
+  const int threads = pairs * tpr;
+  const size_t nblk = G > 1 ? static_cast<size_t>(threads) / G : 0;  // no exchange for blocks inside one thread
+  const size_t smem = 16 * ((3 * pairs * RG * 4 + 15) / 16) + nblk * xgrp(G) * sizeof(T);
+  auto kern = rotq_kernel<DT, CR, MODE, SW, SPLIT>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rotq)");
   }
-  kern<<<L.blocks, L.threads, L.smem, st>>>(x, ldx, static_cast<int>(M), static_cast<int>(K), L.tpr, L.pairs, q, ldq, xs,
-                                            y, ydt, ldy);
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);  // several CTAs' exchange buffers
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+  if (e != cudaSuccess || per_sm < 1) per_sm = 1;
+  const int64_t groups = (M + RG - 1) / RG;
+  const int64_t want = (groups + pairs - 1) / pairs;
+  const int64_t cap = static_cast<int64_t>(sms) * per_sm;
+  const int blocks = static_cast<int>(want < cap ? want : cap);
+  kern<<<blocks, threads, smem, st>>>(x, ldx, static_cast<int>(M), static_cast<int>(K), tpr, pairs, q, ldq, xs, y, ydt, ldy);
   return check_launch("rotq_kernel");
+}
+
+// split mode when both lanes of a thread can be the same row (K a multiple of 32 x the block's threads, <= 512 threads)
+template <int DT, int CR, int MODE, bool SW>
+static int launch_split(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, int64_t ldq, float* xs, void* y,
+                        int ydt, int64_t ldy, cudaStream_t st) {
+  constexpr int G = CR >= 256 ? 16 : (CR == 64 ? 4 : 1);
+  if constexpr (DT != DT_FP32) {
+    if (K % (32 * G) == 0 && K / 32 <= 512) return launch_t<DT, CR, MODE, SW, true>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
+  }
+  return launch_t<DT, CR, MODE, SW, false>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
 }
 
 template <int DT, int MODE, bool SW>
 static int launch_cr(int cr, const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, int64_t ldq, float* xs, void* y,
                      int ydt, int64_t ldy, cudaStream_t st) {
   switch (cr) {
-    case 4: return launch_t<DT, 4, MODE, SW>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
-    case 16: return launch_t<DT, 16, MODE, SW>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
-    case 64: return launch_t<DT, 64, MODE, SW>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
-    case 256: return launch_t<DT, 256, MODE, SW>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
+    case 4: return launch_split<DT, 4, MODE, SW>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
+    case 16: return launch_split<DT, 16, MODE, SW>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
+    case 64: return launch_split<DT, 64, MODE, SW>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
+    case 256: return launch_split<DT, 256, MODE, SW>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
     default: return fail(H3B_ERR_UNSUPPORTED, "convrot must be 4, 16, 64 or 256 on the b200 backend");
   }
 }

@@ -5,6 +5,11 @@
    for every significand pair; rounding to nearest is invariant under scaling by powers of two, so one binade of b per
    divisor covers every normal pair.
 2. The decode level rint(cb * s) clamped to +-127 is what cvt.rni.sat.s8 followed by max(., -127) computes.
+3. For bf16, the quotient only matters after it is rounded to bf16, and RNbf16(RN(b * RN(1/s))) = RNbf16(RN(b / s)) for
+   every pair of bf16 significands: the kernel multiplies by the per-row reciprocal without a correction step.
+4. The bf16 rounding the kernel does on the FMA pipe -- Veltkamp splitting g = v (2^16 + 1), d = v - g, h = g + d, each
+   rounded once -- equals round-to-nearest-even to bf16 for every fp32 significand (ties included) in binades where
+   the intermediates stay normal and finite.
 """
 import math
 from fractions import Fraction as Fr
@@ -60,3 +65,31 @@ def test_decode_level_rule_matches_the_oracle_on_every_fp8_byte():
                                 "fp8", cb, 16)
     assert np.array_equal(grid[:, 0::2], kernel.astype(np.int8))
     assert kernel.min() == -127 and kernel.max() == 127
+
+
+def _rne_bf16(y: np.ndarray) -> np.ndarray:
+    u = y.view(np.uint32)
+    with np.errstate(over="ignore"):
+        return ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)).view(np.float32)
+
+
+def test_veltkamp_split_is_round_to_nearest_even_bf16_for_every_significand():
+    c = np.float32(65537.0)
+    sig = np.arange(1 << 23, dtype=np.uint32)
+    for e in (0, -109, 99):  # the reference binade and both ends of the range the kernel uses it in
+        for sign in (0, 1):
+            y = ((np.uint32(127 + e) << np.uint32(23)) | sig | np.uint32(sign << 31)).view(np.float32)
+            g = (y * c).astype(np.float32)
+            d = (y - g).astype(np.float32)
+            h = (g + d).astype(np.float32)
+            assert np.array_equal(h.view(np.uint32), _rne_bf16(y).view(np.uint32)), (e, sign)
+
+
+def test_reciprocal_product_gives_the_same_bf16_quotient_for_all_bf16_pairs():
+    mb = (np.arange(128, dtype=np.uint32) | 128).astype(np.float32) / np.float32(128.0)
+    r = (np.float32(1.0) / mb).astype(np.float32)
+    for e in range(-3, 9):  # quotients from 2^-4 (code 0) to 2^8 (beyond the clamp)
+        b = (mb * np.float32(2.0 ** e)).astype(np.float32)
+        exact = np.ascontiguousarray((b[:, None] / mb[None, :]).astype(np.float32))
+        fast = np.ascontiguousarray((b[:, None] * r[None, :]).astype(np.float32))
+        assert np.array_equal(_rne_bf16(exact), _rne_bf16(fast)), e
