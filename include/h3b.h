@@ -128,6 +128,34 @@ int h3b_w4a8_gemm_noalloc(const int8_t* qa, int64_t lda, const float* xs, int64_
                           const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N, int64_t K, int quant_mode,
                           void* stream);
 
+/* ---- block streamer: the copy path of StreamingProvider (stream.py:115-623; copies and slot events :333-362,
+ * acquire/release ordering :376-437).  An engine owns a copy stream, per-slot `ready`/`done` events and page-locked host
+ * staging buffers; the caller owns the device slots.  Slot s's copy waits on the device for done[s] (recorded by
+ * release on the compute stream), and acquire makes the compute stream wait for ready[s].  Host waits are bounded. */
+typedef struct h3b_streamer h3b_streamer;
+enum h3b_copy_mode {
+  H3B_COPY_DIRECT = 0,   /* source is page-locked (registered or pinned): one async copy */
+  H3B_COPY_STAGED = 1,   /* pageable source: multi-threaded memcpy into a staging buffer, then an async copy */
+  H3B_COPY_PAGEABLE = 2  /* pageable source copied by the driver (returns once the source has been read) */
+};
+int h3b_streamer_create(int device, int n_slots, int n_staging, size_t staging_bytes, int memcpy_threads,
+                        h3b_streamer** out);
+int h3b_streamer_destroy(h3b_streamer* s);
+int h3b_streamer_copy(h3b_streamer* s, int slot, void* dst, const void* src_host, size_t bytes, int mode);
+/* A caller-driven copy (a custom transfer) on the engine's copy stream: begin (the stream waits for done[slot]),
+ * enqueue the copy on h3b_streamer_stream(s), end (ready[slot] recorded). */
+int h3b_streamer_begin(h3b_streamer* s, int slot);
+int h3b_streamer_end(h3b_streamer* s, int slot, size_t bytes);
+void* h3b_streamer_stream(h3b_streamer* s);
+int h3b_streamer_acquire(h3b_streamer* s, int slot, void* stream);
+int h3b_streamer_release(h3b_streamer* s, int slot, void* stream);
+int h3b_streamer_wait(h3b_streamer* s, int slot, double timeout_s);
+int h3b_streamer_stats(h3b_streamer* s, uint64_t* copies, uint64_t* bytes, double* busy_s);
+/* Page-lock / unlock a host range in place (read_only != 0 for a read-only file mapping: cudaHostRegisterReadOnly).
+ * Replaces the reference's torch.cuda.cudart().cudaHostRegister calls (stream.py:208-217, :232-238). */
+int h3b_host_register(void* ptr, size_t bytes, int read_only);
+int h3b_host_unregister(void* ptr);
+
 /* Device-side failure flag of the current device: a kernel whose bounded wait ran out sets it (and returns instead of
  * hanging).  Returns the flag and, when clear != 0, resets it.  Synchronises the device. */
 int h3b_device_error(int clear);

@@ -21,6 +21,7 @@ NOALLOC_SCRATCH_BYTES = 16 << 20  # H3B_NOALLOC_SCRATCH_BYTES
 OK, ERR_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_DEVICE = 0, 1, 2, 3, 4
 BF16, FP16, FP32, FP8_E4M3, INT32 = 0, 1, 2, 3, 4
 QMODE = {"ck": 0, "eager": 1}
+COPY_DIRECT, COPY_STAGED, COPY_PAGEABLE = 0, 1, 2
 
 _ACT_CODES = {torch.bfloat16: BF16, torch.float16: FP16, torch.float32: FP32}
 _SCALE_CODES = {torch.float8_e4m3fn: FP8_E4M3, torch.uint8: FP8_E4M3, torch.float16: FP16, torch.bfloat16: BF16,
@@ -48,6 +49,19 @@ _SIGNATURES = {
                          _c_void_p, _int, _int, _c_void_p, _c_void_p, _int, _i64, _i64, _int, _c_void_p, _sz, _c_void_p], _int),
     "h3b_w4a8_gemm_noalloc": ([_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _int, _i64, _c_void_p,
                                _c_void_p, _int, _c_void_p, _c_void_p, _int, _i64, _i64, _i64, _int, _c_void_p], _int),
+    "h3b_streamer_create": ([_int, _int, _int, _sz, _int, ctypes.POINTER(ctypes.c_void_p)], _int),
+    "h3b_streamer_destroy": ([_c_void_p], _int),
+    "h3b_streamer_copy": ([_c_void_p, _int, _c_void_p, _c_void_p, _sz, _int], _int),
+    "h3b_streamer_begin": ([_c_void_p, _int], _int),
+    "h3b_streamer_end": ([_c_void_p, _int, _sz], _int),
+    "h3b_streamer_stream": ([_c_void_p], _c_void_p),
+    "h3b_streamer_acquire": ([_c_void_p, _int, _c_void_p], _int),
+    "h3b_streamer_release": ([_c_void_p, _int, _c_void_p], _int),
+    "h3b_streamer_wait": ([_c_void_p, _int, ctypes.c_double], _int),
+    "h3b_streamer_stats": ([_c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                            ctypes.POINTER(ctypes.c_double)], _int),
+    "h3b_host_register": ([_c_void_p, _sz, _int], _int),
+    "h3b_host_unregister": ([_c_void_p], _int),
     "h3b_device_error": ([_int], _int),
 }
 

@@ -30,6 +30,7 @@ int check_launch(const char* what) {
 #include "decode.cuh"
 #include "gemm_sm100.cuh"
 #include "rotq.cuh"
+#include "streamer.cuh"
 
 namespace h3b {
 
@@ -275,6 +276,158 @@ int h3b_w4a8_gemm_noalloc(const int8_t* qa, int64_t lda, const float* xs, int64_
                      bias ? static_cast<const char*>(bias) + static_cast<size_t>(n0) * osz : nullptr,
                      static_cast<char*>(out) + static_cast<size_t>(n0) * osz, out_dtype, ldo, M, nr, K, quant_mode, st);
     if (rc) return rc;
+  }
+  return H3B_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ block streamer
+struct h3b_streamer {
+  h3b::StreamEngine* e;
+};
+
+int h3b_streamer_create(int device, int n_slots, int n_staging, size_t staging_bytes, int memcpy_threads,
+                        h3b_streamer** out) {
+  if (!out || n_slots < 0 || n_staging < 0 || (n_staging > 0 && staging_bytes == 0))
+    return fail(H3B_ERR_ARG, "streamer: need out, n_slots >= 0, n_staging >= 0 and staging_bytes > 0 with staging");
+  *out = nullptr;
+  cudaError_t err = cudaSetDevice(device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaSetDevice");
+  auto* e = new h3b::StreamEngine();
+  e->device = device;
+  e->memcpy_threads = memcpy_threads > 0 ? memcpy_threads : 8;
+  auto bail = [&](cudaError_t er, const char* what) {
+    const int rc = cuda_fail(er, what);
+    h3b::engine_free(e);
+    return rc;
+  };
+  if ((err = cudaStreamCreateWithFlags(&e->copy, cudaStreamNonBlocking)) != cudaSuccess) return bail(err, "cudaStreamCreate");
+  e->ready.assign(n_slots, nullptr);
+  e->done.assign(n_slots, nullptr);
+  e->done_set.assign(n_slots, 0);
+  for (int i = 0; i < n_slots; ++i) {
+    if ((err = cudaEventCreateWithFlags(&e->ready[i], cudaEventDisableTiming)) != cudaSuccess) return bail(err, "cudaEventCreate");
+    if ((err = cudaEventCreateWithFlags(&e->done[i], cudaEventDisableTiming)) != cudaSuccess) return bail(err, "cudaEventCreate");
+  }
+  e->stage_bytes = staging_bytes;
+  for (int i = 0; i < n_staging; ++i) {
+    void* p = nullptr;
+    if ((err = cudaHostAlloc(&p, staging_bytes, cudaHostAllocDefault)) != cudaSuccess) {
+      cudaGetLastError();  // a refused page-lock is not sticky; run with fewer staging buffers
+      break;
+    }
+    e->staging.push_back(p);
+    cudaEvent_t ev;
+    if ((err = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess) return bail(err, "cudaEventCreate");
+    e->stage_ev.push_back(ev);
+    e->stage_used.push_back(0);
+  }
+  *out = new h3b_streamer{e};
+  return H3B_OK;
+}
+
+int h3b_streamer_destroy(h3b_streamer* s) {
+  if (!s) return H3B_OK;
+  h3b::engine_free(s->e);
+  delete s;
+  return H3B_OK;
+}
+
+int h3b_streamer_copy(h3b_streamer* s, int slot, void* dst, const void* src, size_t bytes, int mode) {
+  if (!s || slot < 0 || slot >= static_cast<int>(s->e->ready.size()) || !dst || !src)
+    return fail(H3B_ERR_ARG, "streamer_copy: bad engine, slot or pointer");
+  h3b::StreamEngine* e = s->e;
+  const double t0 = h3b::now_s();
+  cudaError_t err = cudaSetDevice(e->device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaSetDevice");
+  if (mode == H3B_COPY_STAGED && (e->staging.empty() || bytes > e->stage_bytes)) mode = H3B_COPY_PAGEABLE;
+  if (e->done_set[slot] && (err = cudaStreamWaitEvent(e->copy, e->done[slot], 0)) != cudaSuccess)
+    return cuda_fail(err, "cudaStreamWaitEvent(done)");
+  if (mode == H3B_COPY_STAGED) {
+    int k;
+    {
+      std::lock_guard<std::mutex> lock(e->mu);
+      k = e->stage_next;
+      e->stage_next = (k + 1) % static_cast<int>(e->staging.size());
+    }
+    if (e->stage_used[k]) {  // the previous copy out of this staging buffer must have finished
+      const int rc = h3b::event_wait(e->stage_ev[k], 600.0, "streamer staging buffer");
+      if (rc) return rc;
+    }
+    h3b::parallel_memcpy(e->staging[k], src, bytes, e->memcpy_threads);
+    if ((err = cudaMemcpyAsync(dst, e->staging[k], bytes, cudaMemcpyHostToDevice, e->copy)) != cudaSuccess)
+      return cuda_fail(err, "cudaMemcpyAsync(staged)");
+    if ((err = cudaEventRecord(e->stage_ev[k], e->copy)) != cudaSuccess) return cuda_fail(err, "cudaEventRecord");
+    e->stage_used[k] = 1;
+  } else if ((err = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, e->copy)) != cudaSuccess) {
+    return cuda_fail(err, "cudaMemcpyAsync");
+  }
+  if ((err = cudaEventRecord(e->ready[slot], e->copy)) != cudaSuccess) return cuda_fail(err, "cudaEventRecord(ready)");
+  e->copies += 1;
+  e->bytes += bytes;
+  e->busy_ns += static_cast<unsigned long long>((h3b::now_s() - t0) * 1e9);
+  return H3B_OK;
+}
+
+int h3b_streamer_begin(h3b_streamer* s, int slot) {
+  if (!s || slot < 0 || slot >= static_cast<int>(s->e->ready.size())) return fail(H3B_ERR_ARG, "streamer_begin: bad slot");
+  cudaError_t err = cudaSetDevice(s->e->device);
+  if (err == cudaSuccess && s->e->done_set[slot]) err = cudaStreamWaitEvent(s->e->copy, s->e->done[slot], 0);
+  return err == cudaSuccess ? H3B_OK : cuda_fail(err, "streamer_begin");
+}
+
+int h3b_streamer_end(h3b_streamer* s, int slot, size_t bytes) {
+  if (!s || slot < 0 || slot >= static_cast<int>(s->e->ready.size())) return fail(H3B_ERR_ARG, "streamer_end: bad slot");
+  const cudaError_t err = cudaEventRecord(s->e->ready[slot], s->e->copy);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaEventRecord(ready)");
+  s->e->copies += 1;
+  s->e->bytes += bytes;
+  return H3B_OK;
+}
+
+void* h3b_streamer_stream(h3b_streamer* s) { return s ? static_cast<void*>(s->e->copy) : nullptr; }
+
+int h3b_streamer_acquire(h3b_streamer* s, int slot, void* stream) {
+  if (!s || slot < 0 || slot >= static_cast<int>(s->e->ready.size())) return fail(H3B_ERR_ARG, "streamer_acquire: bad slot");
+  const cudaError_t err = cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), s->e->ready[slot], 0);
+  return err == cudaSuccess ? H3B_OK : cuda_fail(err, "cudaStreamWaitEvent(ready)");
+}
+
+int h3b_streamer_release(h3b_streamer* s, int slot, void* stream) {
+  if (!s || slot < 0 || slot >= static_cast<int>(s->e->done.size())) return fail(H3B_ERR_ARG, "streamer_release: bad slot");
+  const cudaError_t err = cudaEventRecord(s->e->done[slot], static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "cudaEventRecord(done)");
+  s->e->done_set[slot] = 1;
+  return H3B_OK;
+}
+
+int h3b_streamer_wait(h3b_streamer* s, int slot, double timeout_s) {
+  if (!s || slot < 0 || slot >= static_cast<int>(s->e->ready.size())) return fail(H3B_ERR_ARG, "streamer_wait: bad slot");
+  return h3b::event_wait(s->e->ready[slot], timeout_s, "streamer copy");
+}
+
+int h3b_streamer_stats(h3b_streamer* s, uint64_t* copies, uint64_t* bytes, double* busy_s) {
+  if (!s) return fail(H3B_ERR_ARG, "streamer_stats: bad engine");
+  if (copies) *copies = s->e->copies.load();
+  if (bytes) *bytes = s->e->bytes.load();
+  if (busy_s) *busy_s = s->e->busy_ns.load() * 1e-9;
+  return H3B_OK;
+}
+
+int h3b_host_register(void* ptr, size_t bytes, int read_only) {
+  if (!ptr || bytes == 0) return fail(H3B_ERR_ARG, "host_register: empty range");
+  const cudaError_t err = cudaHostRegister(ptr, bytes, read_only ? cudaHostRegisterReadOnly : cudaHostRegisterDefault);
+  if (err != cudaSuccess) {
+    cudaGetLastError();  // not sticky: the caller falls back to a pinned copy or staging
+    return cuda_fail(err, "cudaHostRegister");
+  }
+  return H3B_OK;
+}
+
+int h3b_host_unregister(void* ptr) {
+  const cudaError_t err = cudaHostUnregister(ptr);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_fail(err, "cudaHostUnregister");
   }
   return H3B_OK;
 }

@@ -55,3 +55,46 @@ def synthetic_activation(m: int, k: int, *, outlier_frac: float = 0.005, n_outli
     ch = torch.randperm(k, generator=gen, device=dev)[:cnt]
     x[:, ch] *= 20.0
     return x.to(dtype)
+
+
+def synthetic_store_tensors(cfg, *, group: int = 128, scale_dtype: str = "fp16", seed: int = 0, with_globals: bool = True):
+    """Seeded random h3t tensors (ComfyUI-layout names) for a store of cfg.layers W4A8 blocks, each produced lazily while
+    it is written.  Weights are random packed nibbles; group scales fp16 in [8, 15] with the integer codebook (levels up
+    to +-120), or fp8 e4m3 in [20, 200] with a 16-level codebook in [-1, 1] (the real checkpoints' format)."""
+    from .writer import LazySource
+
+    hid, inner, ffn, hd = cfg.hidden, cfg.inner, cfg.ffn, cfg.head_dim
+    fp8 = scale_dtype == "fp8"
+    cb = torch.linspace(-1.0, 1.0, 16) if fp8 else torch.arange(16, dtype=torch.float32) - 8.0
+    linears = {"attn.qkv_proj": (3 * inner, hid), "attn.out_proj": (hid, inner), "mlp.fc1": (2 * ffn, hid), "mlp.fc2": (hid, ffn)}
+    out = {}
+
+    def gen(i: int, salt: int):
+        return torch.Generator().manual_seed(seed * 100003 + i * 97 + salt)
+
+    for i in range(cfg.layers):
+        for j, (name, (n, k)) in enumerate(linears.items()):
+            p = f"blocks.{i}.{name}."
+            out[p + "weight"] = LazySource("I8", (n, k // 2), lambda i=i, j=j, n=n, k=k: torch.empty(n, k // 2, dtype=torch.uint8).random_(generator=gen(i, j)).view(torch.int8))
+            if fp8:
+                out[p + "weight_s_rel"] = LazySource("F8_E4M3", (n, k // group), lambda i=i, j=j, n=n, k=k: (torch.rand(n, k // group, generator=gen(i, 10 + j)) * 180 + 20).to(torch.float8_e4m3fn))
+            else:
+                out[p + "weight_s_rel"] = LazySource("F16", (n, k // group), lambda i=i, j=j, n=n, k=k: (torch.rand(n, k // group, generator=gen(i, 10 + j)) * 7 + 8).to(torch.float16))
+            out[p + "weight_s_channel"] = LazySource("F32", (n,), lambda i=i, j=j, n=n: torch.rand(n, generator=gen(i, 20 + j)) * 4e-4 + 1e-4)
+            out[p + "weight_codebook"] = cb.clone()
+            out[p + "comfy_quant"] = torch.frombuffer(bytearray(f'{{"format":"w4a8_int8","group_size":{group}}}'.encode()), dtype=torch.uint8).clone()
+        for nm, size in (("norm1.weight", hid), ("norm2.weight", hid), ("attn.q_norm.weight", hd), ("attn.k_norm.weight", hd)):
+            out[f"blocks.{i}.{nm}"] = (1.0 + 0.1 * torch.randn(size, generator=gen(i, 30))).to(torch.bfloat16)
+    if with_globals:
+        g = torch.Generator().manual_seed(seed + 7)
+        vp, ac = cfg.video_patch_dim, cfg.audio_channels
+        glob = {"video_patch_proj.weight": (hid, vp), "video_patch_proj.bias": (hid,), "audio_patch_proj.weight": (hid, ac),
+                "audio_patch_proj.bias": (hid,), "condition_proj.weight": (hid, cfg.text_dim), "condition_proj.bias": (hid,),
+                "rope.inv_freq": (cfg.rope_inv_freq_len,), "final_layer.norm.weight": (hid,),
+                "final_layer.adaln_proj.linear.weight": (2 * hid, cfg.t_dim), "final_layer.adaln_proj.linear.bias": (2 * hid,),
+                "final_layer.video_out.weight": (vp, hid), "final_layer.video_out.bias": (vp,),
+                "final_layer.audio_out.weight": (ac, hid), "final_layer.audio_out.bias": (ac,)}
+        for nm, shape in glob.items():
+            dt = torch.bfloat16 if nm in ("condition_proj.weight", "final_layer.norm.weight", "final_layer.adaln_proj.linear.weight") else torch.float32
+            out[nm] = (0.02 * torch.randn(*shape, generator=g)).to(dt)
+    return out
