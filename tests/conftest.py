@@ -32,6 +32,27 @@ def load_package():
 load_package()
 
 
+def _ensure_built():
+    """Build libh3b.so if it is missing, lacks a declared entry point, or (on a machine without a GPU, where the sources
+    are edited) is older than a source.  nvcc cross-compiles for sm_100a without a GPU."""
+    import ctypes
+
+    spec = importlib.util.spec_from_file_location("h3b_build", ROOT / "minimax-h3-turbo_b200" / "build.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    from minimax_h3_turbo_b200 import _lib
+
+    stale = not mod.LIB.exists()
+    if not stale:
+        probe = ctypes.CDLL(str(mod.LIB))
+        stale = any(not hasattr(probe, name) for name in _lib.exported_symbols())
+    if not stale and not has_cuda():
+        stale = not mod.up_to_date()
+    if stale:
+        mod.build()
+
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (a B200) and the built libh3b.so")
 
@@ -54,3 +75,6 @@ def has_cuda():
         return torch.cuda.is_available()
     except Exception:
         return False
+
+
+_ensure_built()
