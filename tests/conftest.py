@@ -43,9 +43,15 @@ def _ensure_built():
     from minimax_h3_turbo_b200 import _lib
 
     stale = not mod.LIB.exists()
-    if not stale:
-        probe = ctypes.CDLL(str(mod.LIB))
-        stale = any(not hasattr(probe, name) for name in _lib.exported_symbols())
+    if not stale:  # probe a copy: loading the real path would pin the old library in this process
+        import shutil
+        import tempfile
+
+        with tempfile.TemporaryDirectory() as d:
+            tmp = Path(d) / "probe.so"
+            shutil.copyfile(mod.LIB, tmp)
+            probe = ctypes.CDLL(str(tmp))
+            stale = any(not hasattr(probe, name) for name in _lib.exported_symbols())
     if not stale and not has_cuda():
         stale = not mod.up_to_date()
     if stale:
