@@ -1,0 +1,194 @@
+"""One single-stream H3 DiT block driven through the W4A8 kernels, optionally token-sharded across GPUs.
+
+Semantics of the reference block (h3turbo/h3/model.py:_block :234-242, _attention :196-228, _mlp :186-194 with
+_rms / _scale_shift_ / _gate_ :64-115 and q/k norm + split-half RoPE, layout.py:norm_rope_ :329-356 in its "torch" form
+:309-326): with AdaLN modulation rows per token segment (precomputed here, as the benchmark configuration states),
+
+    h = rms(x, norm1) * (1 + sc_a) + sh_a                (bf16, in place)
+    q, k, v = qlinear(h, qkv);  q, k <- rope(rms_h(q)), rope(rms_h(k));  o = sdpa(q, k, v)
+    x = x + g_a * qlinear(o, out)
+    h = rms(x, norm2) * (1 + sc_m) + sh_m
+    x = x + g_m * qlinear(qlinear(h, fc1), fc2, input_act="swiglu")
+
+Every linear is the W4A8 qlinear (kernels KA + KB); norms, RoPE, modulation and attention are torch ops (attention
+through torch's SDPA, i.e. the flash / cuDNN library kernels, bf16).
+
+Token sharding (rank r of P owns a contiguous slice of rows): every op above is token-wise except attention, which needs
+all keys and values; each block therefore all-gathers K and V (bf16, [S_local, inner] each) over NCCL before the local
+queries attend, and `gather_rows` assembles the final hidden states at the sequence boundary.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from . import qlinear as ql
+from .types import BlockWeights
+
+Segment = Tuple[int, int, int]  # (first row, end row, modulation row)
+
+
+def rms(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """F.rms_norm over the last dim with the weight in x.dtype (model.py:64-66)."""
+    return F.rms_norm(x, (x.shape[-1],), weight if weight.dtype == x.dtype else weight.to(x.dtype), eps)
+
+
+def rms_lane_order(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """Per-head RMSNorm with the fused kernel's summation order (layout.py:309-326): lane l sums the squares of
+    elements l, l + 32, ... in fp32, then a halving tree over the 32 lanes; x * rsqrt(sum / d + eps) * w rounded once."""
+    d = x.shape[-1]
+    if x.dtype == torch.float32 or d % 32:
+        return F.rms_norm(x, (d,), weight.to(x.dtype), eps)
+    xf = x.to(torch.float32)
+    sq = xf.square().reshape(*x.shape[:-1], d // 32, 32)
+    acc = sq[..., 0, :]
+    for j in range(1, d // 32):
+        acc = acc + sq[..., j, :]
+    for off in (16, 8, 4, 2, 1):
+        acc = acc[..., :off] + acc[..., off:2 * off]
+    return (xf * torch.rsqrt(acc / d + eps) * weight.to(torch.float32)).to(x.dtype)
+
+
+def norm_rope_(x: torch.Tensor, w: torch.Tensor, eps: float, cos: torch.Tensor, sin: torch.Tensor, chunk: int = 4096) -> None:
+    """In place on a [S, heads, D] view: per-head RMSNorm, then the split-half rotation of the first 2 * half channels
+    (angle j pairs channel j with channel j + half), rotation in fp32, rounded once."""
+    half = cos.shape[1]
+    for a in range(0, x.shape[0], chunk):
+        sl = slice(a, a + chunk)
+        xn = rms_lane_order(x[sl], w, eps)
+        c, s = cos[sl].unsqueeze(1).to(torch.float32), sin[sl].unsqueeze(1).to(torch.float32)
+        x1, x2 = xn[..., :half].to(torch.float32), xn[..., half:2 * half].to(torch.float32)
+        o1, o2 = x1 * c - x2 * s, x1 * s + x2 * c
+        xn[..., :half], xn[..., half:2 * half] = o1, o2
+        x[sl] = xn
+
+
+def scale_shift_(h: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, segments: Sequence[Segment]) -> torch.Tensor:
+    for a, b, row in segments:
+        if b > a:
+            h[a:b].mul_(1.0 + scale[row].to(h.dtype)).add_(shift[row].to(h.dtype))
+    return h
+
+
+def gate_(x: torch.Tensor, gate: torch.Tensor, other: torch.Tensor, segments: Sequence[Segment]) -> torch.Tensor:
+    for a, b, row in segments:
+        if b > a:
+            x[a:b].addcmul_(other[a:b], gate[row].to(x.dtype))
+    return x
+
+
+@dataclass
+class Modulation:
+    """AdaLN outputs of one block: six [rows, hidden] tensors (model.py:230-232)."""
+
+    shift_a: torch.Tensor
+    scale_a: torch.Tensor
+    gate_a: torch.Tensor
+    shift_m: torch.Tensor
+    scale_m: torch.Tensor
+    gate_m: torch.Tensor
+
+
+@dataclass
+class ShardSpec:
+    """Token sharding: this rank owns rows [start, stop) of `total`; `group` is the process group (None = one GPU)."""
+
+    start: int
+    stop: int
+    total: int
+    group: Optional[object] = None
+    world: int = 1
+    rank: int = 0
+
+
+def shard_rows(total: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous balanced split: the first total % world ranks get one extra row."""
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def gather_rows(x: torch.Tensor, spec: ShardSpec) -> torch.Tensor:
+    """All-gather of row shards -> [total, ...] on every rank (NCCL all_gather of equal-size, padded buffers)."""
+    if spec.group is None or spec.world == 1:
+        return x
+    import torch.distributed as dist
+
+    sizes = [b - a for a, b in (shard_rows(spec.total, spec.world, r) for r in range(spec.world))]
+    cap = max(sizes)
+    buf = torch.empty(cap, *x.shape[1:], dtype=x.dtype, device=x.device)
+    buf[: x.shape[0]] = x
+    out = torch.empty(spec.world * cap, *x.shape[1:], dtype=x.dtype, device=x.device)
+    if dist.get_backend(spec.group) == "nccl":
+        dist.all_gather_into_tensor(out, buf, group=spec.group)
+    else:  # gloo (CPU ranks): list form
+        dist.all_gather(list(out.chunk(spec.world)), buf, group=spec.group)
+    if all(s == cap for s in sizes):
+        return out
+    return torch.cat([out[r * cap: r * cap + sizes[r]] for r in range(spec.world)])
+
+
+class DiTBlock:
+    """Runs H3 DiT blocks on the W4A8 kernels.  heads / head_dim / eps as in H3Config."""
+
+    def __init__(self, heads: int, head_dim: int, norm_eps: float = 1e-5, qk_norm_eps: float = 1e-5,
+                 precision: str = "a8", attn_chunk: Optional[int] = None, linear=None):
+        self.heads, self.head_dim = heads, head_dim
+        self.norm_eps, self.qk_norm_eps, self.precision = norm_eps, qk_norm_eps, precision
+        self.attn_chunk = attn_chunk
+        # the linear op: the W4A8 qlinear (default); tests of the token-sharding plumbing on CPU ranks pass a dense one
+        self._linear = linear or (lambda x, w, input_act=None: ql.linear(x, w, precision=self.precision, input_act=input_act))
+
+    def attention(self, h: torch.Tensor, w: BlockWeights, cos: torch.Tensor, sin: torch.Tensor,
+                  spec: Optional[ShardSpec] = None) -> torch.Tensor:
+        s, heads, hd = h.shape[0], self.heads, self.head_dim
+        inner = heads * hd
+        qkv = self._linear(h, w.qkv)
+        q, k, v = (t.view(s, heads, hd) for t in qkv.split(inner, dim=-1))
+        norm_rope_(q, w.q_norm, self.qk_norm_eps, cos, sin)
+        norm_rope_(k, w.k_norm, self.qk_norm_eps, cos, sin)
+        if spec is not None and spec.world > 1:  # every query needs every key and value
+            k = gather_rows(k.reshape(s, inner).contiguous(), spec).view(-1, heads, hd)
+            v = gather_rows(v.reshape(s, inner).contiguous(), spec).view(-1, heads, hd)
+        qh = q.transpose(0, 1).unsqueeze(0)
+        kh, vh = (t.transpose(0, 1).unsqueeze(0) for t in (k, v))
+        step = self.attn_chunk or s
+        if step >= s:
+            o = F.scaled_dot_product_attention(qh, kh, vh).transpose(1, 2).reshape(s, inner)
+        else:  # query rows are independent: chunking is exact
+            o = torch.empty(s, inner, dtype=h.dtype, device=h.device)
+            for a in range(0, s, step):
+                o[a:a + step] = F.scaled_dot_product_attention(qh[:, :, a:a + step], kh, vh)[0].transpose(0, 1).reshape(-1, inner)
+        return self._linear(o, w.out)
+
+    def mlp(self, h: torch.Tensor, w: BlockWeights) -> torch.Tensor:
+        return self._linear(self._linear(h, w.fc1), w.fc2, input_act="swiglu")
+
+    def __call__(self, x: torch.Tensor, w: BlockWeights, mod: Modulation, segments: Sequence[Segment], cos: torch.Tensor,
+                 sin: torch.Tensor, spec: Optional[ShardSpec] = None) -> torch.Tensor:
+        """x: [S_local, hidden] residual stream (updated in place and returned); cos/sin: [S_local, half] for these rows."""
+        h = scale_shift_(rms(x, w.norm1, self.norm_eps), mod.shift_a, mod.scale_a, segments)
+        gate_(x, mod.gate_a, self.attention(h, w, cos, sin, spec), segments)
+        h = scale_shift_(rms(x, w.norm2, self.norm_eps), mod.shift_m, mod.scale_m, segments)
+        return gate_(x, mod.gate_m, self.mlp(h, w), segments)
+
+
+def rope_tables(positions: torch.Tensor, inv_freq: torch.Tensor, dtype: torch.dtype) -> Tuple[torch.Tensor, torch.Tensor]:
+    """[S, 3] (t, h, w) positions -> cos, sin [S, 3 F] in `dtype` (layout.py:265-273: all t frequencies, then h, then w)."""
+    ang = (positions.to(torch.float32).unsqueeze(-1) * inv_freq.to(torch.float32).view(1, 1, -1)).reshape(positions.shape[0], -1)
+    return ang.cos().to(dtype), ang.sin().to(dtype)
+
+
+def video_audio_positions(frames: int, h: int, w: int, audio: int, device) -> torch.Tensor:
+    """Token positions of a packed video (frames x h x w patches) + audio sequence: video tokens get (t, y, x), audio
+    tokens (t, 0, 0) -- the layout of the benchmark's single-stream block."""
+    t = torch.arange(frames, device=device).view(-1, 1, 1).expand(frames, h, w)
+    y = torch.arange(h, device=device).view(1, -1, 1).expand(frames, h, w)
+    xx = torch.arange(w, device=device).view(1, 1, -1).expand(frames, h, w)
+    vid = torch.stack([t, y, xx], -1).reshape(-1, 3)
+    aud = torch.stack([torch.arange(audio, device=device), torch.zeros(audio, device=device, dtype=torch.long),
+                       torch.zeros(audio, device=device, dtype=torch.long)], -1)
+    return torch.cat([vid, aud]).to(torch.float32)
