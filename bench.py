@@ -36,6 +36,14 @@ ROOT = Path(__file__).resolve().parent
 SWEEP = [(5120, 5120), (5120, 13824), (13824, 5120)]  # (K, N)
 MS = [256, 2048, 16384, 65536]
 METRIC = "W4A8 qlinear int8 TOPS"
+WORKLOADS = ("sweep", "block", "stream", "longseq")
+HID, HEADS, HEAD_DIM, FFN = 5120, 40, 128, 13824  # DiT width, attention heads x head dim, SwiGLU width
+BLOCK_LINEARS = [(HID, 3 * HID), (HID, HID), (HID, 2 * FFN), (FFN, HID)]  # (K, N): qkv, out, fc1, fc2 (SwiGLU input)
+BLOCK_OPS_PER_TOKEN = sum(2.0 * k * n for k, n in BLOCK_LINEARS)  # 634.4 M
+# token sequences: latent frames x patch rows x patch cols of video + audio tokens, and how many blocks run on them
+SEQS = {"block": (31, 26, 15, 200, 1),  # 5 s 832x480: 12090 + 200 = 12290 tokens, one block
+        "longseq": (241, 20, 12, 1600, 4)}  # 40 s 640x384: 57840 + 1600 = 59440 tokens, four blocks
+STREAM_BLOCKS, STREAM_TOKENS, STREAM_RESIDENT, STREAM_RING, STREAM_PREFETCH = 48, 4096, 4, 3, 2
 
 
 def load_package():
@@ -135,17 +143,15 @@ class ClockSampler:
 _CPU_WEIGHTS = {}
 
 
-def cpu_reference_rate(ms, rows: int, reps: int = 1, seed: int = 0):
-    """The reference's CPU algorithm (oracle port) on a bounded sample: per projection, one full weight decode (the
-    reference decodes on every call) plus quantise + exact int8 GEMM + epilogue on `rows` rows.  Extrapolated per token
-    (token-wise path) to the sweep: t(M) = t_decode + M * t_row.  Returns (TOPS, detail)."""
-    import numpy as np
-
+def cpu_projection_times(projs, rows: int, reps: int = 1, seed: int = 0):
+    """The reference's CPU algorithm (oracle port) on a bounded sample: per (K, N) projection, one full weight decode (the
+    reference decodes on every call) plus quantise + exact int8 GEMM + epilogue on `rows` rows.  Returns
+    [(K, N, t_decode_s, t_per_row_s)]: the path is token-wise, so a call on M rows costs t_decode + M * t_per_row."""
     sys.path.insert(0, str(ROOT))
     from oracle import qlinear_oracle as orc
 
-    total_t, detail = 0.0, []
-    for (k, n) in SWEEP:
+    res = []
+    for (k, n) in projs:
         key = (k, n, seed)
         if key not in _CPU_WEIGHTS:  # generated once per process, outside the timed part
             _CPU_WEIGHTS[key] = orc.synth_weight_int4_g128(n, k, seed=seed + k + n)
@@ -162,18 +168,35 @@ def cpu_reference_rate(ms, rows: int, reps: int = 1, seed: int = 0):
             t2 = time.perf_counter()
             t_dec.append(t1 - t0)
             t_rows.append((t2 - t1) / rows)
-        td, tr = min(t_dec), min(t_rows)
-        for m in ms:
-            total_t += td + m * tr
+        res.append((k, n, min(t_dec), min(t_rows)))
+    return res
+
+
+def cpu_reference_rate(ms, rows: int, reps: int = 1, seed: int = 0):
+    """CPU TOPS of the sweep, extrapolated per token from cpu_projection_times.  Returns (TOPS, detail)."""
+    total_t, detail = 0.0, []
+    for (k, n, td, tr) in cpu_projection_times(SWEEP, rows, reps, seed):
+        total_t += sum(td + m * tr for m in ms)
         detail.append({"K": k, "N": n, "decode_s": round(td, 4), "per_row_ms": round(tr * 1e3, 4)})
     return ops_of(sweep_points(ms)) / total_t / 1e12, detail
+
+
+def cpu_block_rate(tokens: int, n_blocks: int, rows: int):
+    """CPU tokens/s of n_blocks DiT blocks on `tokens` rows counting only the four W4A8 linears (attention, norms and
+    RoPE excluded, so this is an upper bound on the CPU block rate), extrapolated per token.  Returns (tokens/s, detail)."""
+    total_t, detail = 0.0, []
+    for (k, n, td, tr) in cpu_projection_times(BLOCK_LINEARS, rows):
+        total_t += n_blocks * (td + tokens * tr)
+        detail.append({"K": k, "N": n, "decode_s": round(td, 4), "per_row_ms": round(tr * 1e3, 4)})
+    return tokens / total_t, detail
 
 
 def run_reference(args, rank):
     if rank != 0:
         return
-    import numpy as np  # noqa: F401
-
+    if args.workload != "sweep":
+        run_reference_dit(args)
+        return
     cores = os.cpu_count() or 1
     ms = args.ms
     rows = args.ref_rows
@@ -202,7 +225,398 @@ def config_dict(ms, world):
             "parallelism": f"token-shard x{world}", "l2": "inputs larger than L2 (each step streams ~8 GB)"}
 
 
-# ------------------------------------------------------------------------------------------------ GPU leg
+def dit_shape(workload):
+    """(tokens, blocks, video tokens, metric, config) of a DiT workload."""
+    if workload == "stream":
+        t, nb, vid = STREAM_TOKENS, STREAM_BLOCKS, STREAM_TOKENS
+        cfg = {"workload": f"config4 weight streaming: {nb} W4A8 DiT blocks (width {HID}, {HEADS}x{HEAD_DIM} heads, "
+                           f"FFN {FFN} SwiGLU) held in a pinned host h3t store, {STREAM_RESIDENT} resident + a "
+                           f"{STREAM_RING}-slot ring on the GPU, prefetch {STREAM_PREFETCH}; M={t} tokens",
+               "model": "H3 DiT block stack, W4A8 int4 group-128 fp16 scales", "tokens": t, "blocks": nb}
+        return t, nb, vid, "DiT 48-block stack tokens/s, weights streamed from pinned host", cfg
+    f, h, w, audio, nb = SEQS[workload]
+    vid = f * h * w
+    t = vid + audio
+    name = "config3 one DiT block" if workload == "block" else "config5 long sequence, 4 DiT blocks"
+    cfg = {"workload": f"{name}: M={t} tokens ({f}x{h}x{w} video + {audio} audio), width {HID}, {HEADS}x{HEAD_DIM} heads, "
+                       f"FFN {FFN} SwiGLU, W4A8 linears, bf16 attention/norms, AdaLN modulation precomputed",
+           "model": "H3 DiT block, W4A8 int4 group-128 fp16 scales", "tokens": t, "blocks": nb}
+    return t, nb, vid, f"DiT block tokens/s ({name})", cfg
+
+
+def run_reference_dit(args):
+    tokens, nb, _, metric, cfg = dit_shape(args.workload)
+    cores = os.cpu_count() or 1
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, detail = cpu_block_rate(tokens, nb, args.ref_rows)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    cfg = dict(cfg, parallelism=f"{args.gpus} GPU(s) requested; the CPU arm runs on rank 0's host cores")
+    line = {"metric": metric, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": tokens / value * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": f"the four W4A8 linears only (attention, norms, RoPE excluded: an upper bound), "
+                                       f"{args.ref_rows} rows per projection + one full weight decode, per-token "
+                                       f"extrapolation to {tokens} tokens x {nb} blocks ({cores} threads)",
+                             "detail": detail},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ DiT workloads (GPU)
+def synthetic_block(seed, dev):
+    """Random W4A8 block at DiT width (int4 group-128 from N(0, 0.02), fp16 scales) with bf16 norm weights."""
+    import torch
+    from minimax_h3_turbo_b200.h3.synth import synthetic_w4a8
+    from minimax_h3_turbo_b200.h3.types import BlockWeights
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    norm = lambda n: (1.0 + 0.1 * torch.randn(n, generator=g, device=dev)).to(torch.bfloat16)  # noqa: E731
+    lin = [synthetic_w4a8(n, k, seed=seed * 10 + j, device=dev) for j, (k, n) in enumerate(BLOCK_LINEARS)]
+    return BlockWeights(qkv=lin[0], out=lin[1], fc1=lin[2], fc2=lin[3], norm1=norm(HID), norm2=norm(HID),
+                        q_norm=norm(HEAD_DIM), k_norm=norm(HEAD_DIM))
+
+
+def synthetic_modulation(seed, dev):
+    """Precomputed AdaLN outputs: six [2, HID] bf16 N(0, 1) rows (row 0: video tokens, row 1: audio tokens)."""
+    import torch
+    from minimax_h3_turbo_b200.h3 import block as blk
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return blk.Modulation(*(torch.randn(2, HID, generator=g, device=dev).to(torch.bfloat16) for _ in range(6)))
+
+
+def dit_sequence(frames, hh, ww, audio, start, stop, dev):
+    """RoPE tables and modulation segments of rows [start, stop) of a video + audio token sequence."""
+    import torch
+    from minimax_h3_turbo_b200.h3 import block as blk
+
+    pos = blk.video_audio_positions(frames, hh, ww, audio, dev)[start:stop]
+    inv_freq = 1.0 / (10000.0 ** (torch.arange(16, device=dev, dtype=torch.float32) / 16))
+    cos, sin = blk.rope_tables(pos, inv_freq, torch.bfloat16)
+    vid = frames * hh * ww
+    segs = []
+    for a, b, row in ((0, vid, 0), (vid, vid + audio, 1)):
+        a, b = max(a, start), min(b, stop)
+        if b > a:
+            segs.append((a - start, b - start, row))
+    return cos, sin, segs
+
+
+class TimedLinear:
+    """The W4A8 qlinear with CUDA events around each call on the launching stream (when `on`)."""
+
+    def __init__(self):
+        from minimax_h3_turbo_b200.h3 import qlinear as ql
+
+        self.ql, self.on, self.events, self.calls = ql, False, [], 0
+
+    def __call__(self, x, w, input_act=None):
+        import torch
+
+        if not self.on:
+            return self.ql.linear(x, w, input_act=input_act)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        y = self.ql.linear(x, w, input_act=input_act)
+        e1.record()
+        self.events.append((e0, e1))
+        self.calls += 1
+        return y
+
+    def ms(self):
+        return sum(a.elapsed_time(b) for a, b in self.events)
+
+
+def dit_common_fields(pk, lin_ops, lin_ms, attn_flops, total_ms, steps):
+    """Roofline of the qlinear share and of the block as a whole (per rank, per step)."""
+    int8_peak, bf16_peak = 2.0 * pk["bf16"], pk["bf16"]
+    lin_tops = lin_ops / (lin_ms / steps * 1e-3) / 1e12 if lin_ms > 0 else None
+    bound_ms = (lin_ops / (int8_peak * 1e12) + attn_flops / (bf16_peak * 1e12)) * 1e3
+    rest_ms = (total_ms - lin_ms) / steps
+    return {"roofline": {"bound": "tensor", "kernel": "W4A8 qlinear (rotq + decode + gemm_i8 per call)", "achieved": lin_tops,
+                         "peak": int8_peak, "unit": "TOPS", "frac": lin_tops / int8_peak if lin_tops else None, "traffic": None,
+                         "peak_note": f"int8 dense = 2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s burst)"},
+            "block_roofline": {"bound_ms": bound_ms, "measured_ms": total_ms / steps, "frac": bound_ms / (total_ms / steps),
+                               "basis": "linear ops / int8 peak + attention flops / bf16 peak, per rank per step"},
+            "split_ms_per_step": {"qlinear": lin_ms / steps, "attention_norms_rope_gathers": rest_ms,
+                                  "attention_tflops_if_all_rest": attn_flops / (rest_ms * 1e-3) / 1e12 if rest_ms > 0 else None}}
+
+
+def run_dit(args, rank, world, local):
+    """Configs 3 and 5: DiT blocks on a video + audio sequence, token-sharded over the ranks (K/V all-gathered per
+    block, the final hidden states all-gathered at the sequence boundary)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    load_package()
+    from minimax_h3_turbo_b200.h3 import block as blk
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    frames, hh, ww, audio, nb = SEQS[args.workload]
+    tokens, _, _, metric, cfg = dit_shape(args.workload)
+    a, b = blk.shard_rows(tokens, world, rank)
+    spec = blk.ShardSpec(a, b, tokens, group=dist.group.WORLD if world > 1 else None, world=world, rank=rank)
+    cos, sin, segs = dit_sequence(frames, hh, ww, audio, a, b, dev)
+    weights = [synthetic_block(100 + i, dev) for i in range(nb)]  # the same seeds on every rank: replicated weights
+    mods = [synthetic_modulation(200 + i, dev) for i in range(nb)]
+    gx = torch.Generator(device=dev).manual_seed(7)
+    x0 = torch.randn(tokens, HID, generator=gx, device=dev).to(torch.bfloat16)[a:b].contiguous()
+    x = torch.empty_like(x0)
+    lin = TimedLinear()
+    block = blk.DiTBlock(HEADS, HEAD_DIM, linear=lin)
+    stream = torch.cuda.current_stream(dev)
+
+    def forward(xin):
+        x.copy_(xin)
+        y = x
+        for i in range(nb):
+            y = block(y, weights[i], mods[i], segs, cos, sin, spec)
+        return blk.gather_rows(y, spec)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        forward(x0)
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    lin.on = True
+    t0.record(stream)
+    for _ in range(args.steps):
+        out = forward(x0)
+    t1.record(stream)
+    barrier()
+    lin.on = False
+    clk = clocks.stop()
+    t_local = torch.tensor([t0.elapsed_time(t1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
+    t_ms = float(t_local.item())
+    finite = bool(torch.isfinite(out.float()).all().item()) and tuple(out.shape) == (tokens, HID)
+
+    # e2e: this rank's input rows from pinned host memory, the gathered output back to pinned host memory (rank 0)
+    e2e = None
+    if not args.no_e2e:
+        hin = torch.empty(b - a, HID, dtype=torch.bfloat16, pin_memory=True)
+        hin.copy_(x0)
+        hout = torch.empty(tokens, HID, dtype=torch.bfloat16, pin_memory=True)
+        e_steps = max(1, min(args.steps, 2))
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e_steps):
+            y = forward(hin.to(dev, non_blocking=True))
+            if rank == 0:
+                hout.copy_(y, non_blocking=True)
+        e1.record(stream)
+        barrier()
+        te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": tokens * e_steps / (float(te.item()) * 1e-3), "unit": "tokens/s",
+               "h2d_bytes_per_step": tokens * HID * 2, "d2h_bytes_per_step": tokens * HID * 2, "steps": e_steps,
+               "path": "DiTBlock over qlinear.linear; each rank copies its input rows in from pinned host memory, rank 0 "
+                       "copies the gathered [tokens, 5120] output out"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        v, detail = cpu_block_rate(tokens, nb, args.cpu_rows)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"the four W4A8 linears only (attention, norms, RoPE excluded: an upper bound), {args.cpu_rows} "
+                         f"rows per projection + one full weight decode, per-token extrapolation ({cores} threads)",
+               "detail": detail}
+
+    rows = b - a
+    lin_ops = nb * rows * BLOCK_OPS_PER_TOKEN
+    attn_flops = nb * 4.0 * rows * tokens * HEADS * HEAD_DIM
+    fields = dit_common_fields(peaks(), lin_ops, lin.ms(), attn_flops, t_ms if world == 1 else t0.elapsed_time(t1), args.steps)
+    if rank == 0:
+        cfg = dict(cfg, parallelism=f"token-shard x{world} (contiguous rows, K/V all-gather per block, output all-gather)",
+                   rows_per_rank=[e - s for s, e in (blk.shard_rows(tokens, world, r) for r in range(world))],
+                   l2="inputs larger than L2 (each block streams ~0.6 GB of weights+activations per rank)")
+        line = {"metric": metric, "value": tokens * args.steps / (t_ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": cfg, **fields,
+                "linear_tops_whole_job": world * lin_ops * args.steps / (t_ms * 1e-3) / 1e12,
+                "output_finite": finite, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "gpu_launches": 3 * lin.calls}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def pick_store_dir(need_bytes, want=None):
+    import shutil
+    import tempfile
+
+    cands = [want] if want else [tempfile.gettempdir(), "/dev/shm", str(ROOT)]
+    for d in cands:
+        try:
+            if d and os.path.isdir(d) and shutil.disk_usage(d).free > 1.1 * need_bytes:
+                return Path(d)
+        except OSError:
+            continue
+    raise SystemExit(f"bench.py: no directory among {cands} has {need_bytes / 1e9:.1f} GB free for the h3t store")
+
+
+def run_stream(args, rank, world, local):
+    """Config 4: a 48-block stack from a pinned host h3t store through the StreamingProvider (4 resident blocks + a
+    3-slot ring), against the same stack fully resident, a copy-only pass, and a pinned host->device copy peak."""
+    if world > 1:
+        raise SystemExit("bench.py: the stream workload runs on one GPU (each rank would need its own host store)")
+    import torch
+
+    load_package()
+    from minimax_h3_turbo_b200.h3 import block as blk
+    from minimax_h3_turbo_b200.h3 import stream as sm
+    from minimax_h3_turbo_b200.h3.config import H3Config
+    from minimax_h3_turbo_b200.h3.store import H3TFile
+    from minimax_h3_turbo_b200.h3.synth import synthetic_store_tensors
+    from minimax_h3_turbo_b200.h3.writer import write_h3t
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    tokens, nb, _, metric, cfgd = dit_shape("stream")
+    hcfg = H3Config(hidden=HID, layers=nb, refiner_layers=0, heads=HEADS, head_dim=HEAD_DIM, ffn=FFN, quant_group=128)
+    est = nb * 164e6
+    path = pick_store_dir(est, args.store_dir) / f"h3b_bench_stack_{os.getpid()}.h3t"
+    tw = time.perf_counter()
+    write_h3t(path, hcfg, synthetic_store_tensors(hcfg, group=128, scale_dtype="fp16", seed=11, with_globals=False, device=dev),
+              quant={"format": "asym_w4a8_int8", "group_size": 128, "convrot_groupsize": 256})
+    write_s = time.perf_counter() - tw
+    store = H3TFile(path)
+    try:
+        mod = synthetic_modulation(300, dev)
+        f, h, w = 16, 16, 16  # 4096 video tokens
+        cos, sin, segs = dit_sequence(f, h, w, 0, 0, tokens, dev)
+        x0 = torch.randn(tokens, HID, generator=torch.Generator(device=dev).manual_seed(5), device=dev).to(torch.bfloat16)
+        x = torch.empty_like(x0)
+        block = blk.DiTBlock(HEADS, HEAD_DIM)
+
+        def forward(p, compute=True):
+            x.copy_(x0)
+            y = x
+            p.begin_forward()
+            for i in range(nb):
+                wi = p.acquire(i)
+                if compute:
+                    y = block(y, wi, mod, segs, cos, sin)
+                p.release(i)
+            p.end_forward()
+            return y
+
+        def timed(p, compute=True, clocks=None):
+            for _ in range(args.warmup):
+                forward(p, compute)
+            torch.cuda.synchronize(dev)
+            s0 = p.stats()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if clocks:
+                clocks.start()
+            e0.record(stream)
+            for _ in range(args.steps):
+                y = forward(p, compute)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            clk = clocks.stop() if clocks else None
+            s1 = p.stats()
+            d = {k: s1[k] - s0[k] for k in ("acquires", "waits", "wait_s", "copies", "bytes")}
+            return e0.elapsed_time(e1) / args.steps, d, y, clk
+
+        # pinned host -> device link peak: one cudaMemcpyAsync of 1 GiB from pinned memory, best of 5
+        hb = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+        db = torch.empty_like(hb, device=dev)
+        best = float("inf")
+        for _ in range(6):
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(stream)
+            db.copy_(hb, non_blocking=True)
+            c1.record(stream)
+            torch.cuda.synchronize(dev)
+            best = min(best, c0.elapsed_time(c1))
+        link_gbs = hb.numel() / (best * 1e-3) / 1e9
+        del hb, db
+
+        clocks = ClockSampler(local)
+        with sm.StreamingProvider(store, dev, resident=STREAM_RESIDENT, ring=STREAM_RING, prefetch=STREAM_PREFETCH,
+                                  pin=True) as p:
+            t_stream, d_stream, y_stream, clk = timed(p, True, clocks)
+            t_copy, d_copy, _, _ = timed(p, False)
+            kinds = sorted(set(p.stats()["host_kinds"]))
+            # e2e through the public API: activations in from pinned host memory, the result back out
+            hin = torch.empty(tokens, HID, dtype=torch.bfloat16, pin_memory=True)
+            hin.copy_(x0)
+            hout = torch.empty_like(hin)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e_steps = max(1, min(args.steps, 2))
+            e0.record(stream)
+            for _ in range(e_steps):
+                x0.copy_(hin, non_blocking=True)
+                hout.copy_(forward(p, True), non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            t_e2e = e0.elapsed_time(e1) / e_steps
+        with sm.StreamingProvider(store, dev, resident=nb, ring=1, prefetch=0, pin=False) as p:
+            t_res, _, y_res, _ = timed(p, True)
+        same = bool(torch.equal(y_stream, y_res))
+        nbytes = store.block_nbytes
+    finally:
+        store.close()
+        path.unlink(missing_ok=True)
+
+    h2d_gbs = d_stream["bytes"] / args.steps / (t_stream * 1e-3) / 1e9
+    copy_gbs = d_copy["bytes"] / args.steps / (t_copy * 1e-3) / 1e9
+    pk = peaks()
+    lin_ops = nb * tokens * BLOCK_OPS_PER_TOKEN
+    cpu = None
+    if not args.no_cpu:
+        cores = os.cpu_count() or 1
+        v, detail = cpu_block_rate(tokens, nb, args.cpu_rows)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"the four W4A8 linears only (attention, norms excluded: an upper bound), {args.cpu_rows} rows per "
+                         f"projection + one full weight decode, per-token extrapolation to {nb} blocks ({cores} threads)",
+               "detail": detail}
+    cfgd = dict(cfgd, block_nbytes=nbytes, store_bytes=nb * nbytes, host_kinds=kinds, store_write_s=round(write_s, 1),
+                parallelism="one GPU")
+    line = {"metric": metric, "value": tokens / (t_stream * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_stream, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic", "config": cfgd,
+            "roofline": {"bound": "h2d", "kernel": "host->device block copies (copy engine)", "achieved": h2d_gbs,
+                         "peak": link_gbs, "unit": "GB/s", "frac": h2d_gbs / link_gbs, "traffic": None,
+                         "peak_note": "pinned 1 GiB cudaMemcpyAsync measured in this run"},
+            "streaming": {"ms_per_forward_streamed": t_stream, "ms_per_forward_resident": t_res,
+                          "ms_per_forward_copy_only": t_copy, "streamed_vs_resident": t_res / t_stream,
+                          "hidden_copy_frac": 1.0 - (t_stream - t_res) / t_copy, "h2d_gbs_streamed": h2d_gbs,
+                          "h2d_gbs_copy_only": copy_gbs, "link_peak_gbs": link_gbs,
+                          "bytes_per_forward": d_stream["bytes"] / args.steps, "waits_per_forward": d_stream["waits"] / args.steps,
+                          "wait_s_per_forward": d_stream["wait_s"] / args.steps, "streamed_equals_resident": same,
+                          "linear_tops_resident": lin_ops / (t_res * 1e-3) / 1e12, "int8_peak": 2.0 * pk["bf16"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": tokens / (t_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": tokens * HID * 2,
+                    "d2h_bytes_per_step": tokens * HID * 2, "steps": e_steps,
+                    "path": "activations in from pinned host memory, 48 streamed blocks, result out to pinned host memory"},
+            "clocks": clk, "gpu_launches": 12 * nb * args.steps}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ GPU leg: the sweep
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -215,6 +629,9 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--ref-rows", type=int, default=256)
     ap.add_argument("--detail", default="", help="write per-point timings to this JSON file")
+    ap.add_argument("--workload", default="sweep", choices=WORKLOADS,
+                    help="sweep: config 2 (default); block: config 3; stream: config 4; longseq: config 5")
+    ap.add_argument("--store-dir", default="", help="stream workload: directory for the temporary ~7.9 GB h3t store")
     args = ap.parse_args()
     args.ms = [int(v) for v in args.ms.split(",") if v]
     rank, world, local = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
@@ -224,7 +641,16 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
+    if args.workload in ("block", "longseq"):
+        run_dit(args, rank, world, local)
+        return
+    if args.workload == "stream":
+        run_stream(args, rank, world, local)
+        return
+    run_sweep(args, rank, world, local)
 
+
+def run_sweep(args, rank, world, local):
     import torch
     import torch.distributed as dist
     from datetime import timedelta

@@ -57,10 +57,13 @@ def synthetic_activation(m: int, k: int, *, outlier_frac: float = 0.005, n_outli
     return x.to(dtype)
 
 
-def synthetic_store_tensors(cfg, *, group: int = 128, scale_dtype: str = "fp16", seed: int = 0, with_globals: bool = True):
+def synthetic_store_tensors(cfg, *, group: int = 128, scale_dtype: str = "fp16", seed: int = 0, with_globals: bool = True,
+                            device="cpu"):
     """Seeded random h3t tensors (ComfyUI-layout names) for a store of cfg.layers W4A8 blocks, each produced lazily while
     it is written.  Weights are random packed nibbles; group scales fp16 in [8, 15] with the integer codebook (levels up
-    to +-120), or fp8 e4m3 in [20, 200] with a 16-level codebook in [-1, 1] (the real checkpoints' format)."""
+    to +-120), or fp8 e4m3 in [20, 200] with a 16-level codebook in [-1, 1] (the real checkpoints' format).  `device`:
+    where the random linear-layer tensors are drawn (a GPU generates multi-GB stores fast); they are written from host
+    copies, and the values depend on the device."""
     from .writer import LazySource
 
     hid, inner, ffn, hd = cfg.hidden, cfg.inner, cfg.ffn, cfg.head_dim
@@ -69,17 +72,19 @@ def synthetic_store_tensors(cfg, *, group: int = 128, scale_dtype: str = "fp16",
     linears = {"attn.qkv_proj": (3 * inner, hid), "attn.out_proj": (hid, inner), "mlp.fc1": (2 * ffn, hid), "mlp.fc2": (hid, ffn)}
     out = {}
 
-    def gen(i: int, salt: int):
-        return torch.Generator().manual_seed(seed * 100003 + i * 97 + salt)
+    dev = torch.device(device)
+
+    def gen(i: int, salt: int, on=None):
+        return torch.Generator(device=on or "cpu").manual_seed(seed * 100003 + i * 97 + salt)
 
     for i in range(cfg.layers):
         for j, (name, (n, k)) in enumerate(linears.items()):
             p = f"blocks.{i}.{name}."
-            out[p + "weight"] = LazySource("I8", (n, k // 2), lambda i=i, j=j, n=n, k=k: torch.empty(n, k // 2, dtype=torch.uint8).random_(generator=gen(i, j)).view(torch.int8))
+            out[p + "weight"] = LazySource("I8", (n, k // 2), lambda i=i, j=j, n=n, k=k: torch.empty(n, k // 2, dtype=torch.uint8, device=dev).random_(generator=gen(i, j, dev)).view(torch.int8).cpu())
             if fp8:
-                out[p + "weight_s_rel"] = LazySource("F8_E4M3", (n, k // group), lambda i=i, j=j, n=n, k=k: (torch.rand(n, k // group, generator=gen(i, 10 + j)) * 180 + 20).to(torch.float8_e4m3fn))
+                out[p + "weight_s_rel"] = LazySource("F8_E4M3", (n, k // group), lambda i=i, j=j, n=n, k=k: (torch.rand(n, k // group, generator=gen(i, 10 + j, dev), device=dev) * 180 + 20).to(torch.float8_e4m3fn).cpu())
             else:
-                out[p + "weight_s_rel"] = LazySource("F16", (n, k // group), lambda i=i, j=j, n=n, k=k: (torch.rand(n, k // group, generator=gen(i, 10 + j)) * 7 + 8).to(torch.float16))
+                out[p + "weight_s_rel"] = LazySource("F16", (n, k // group), lambda i=i, j=j, n=n, k=k: (torch.rand(n, k // group, generator=gen(i, 10 + j, dev), device=dev) * 7 + 8).to(torch.float16).cpu())
             out[p + "weight_s_channel"] = LazySource("F32", (n,), lambda i=i, j=j, n=n: torch.rand(n, generator=gen(i, 20 + j)) * 4e-4 + 1e-4)
             out[p + "weight_codebook"] = cb.clone()
             out[p + "comfy_quant"] = torch.frombuffer(bytearray(f'{{"format":"w4a8_int8","group_size":{group}}}'.encode()), dtype=torch.uint8).clone()
