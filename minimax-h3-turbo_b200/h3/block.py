@@ -158,7 +158,7 @@ class DiTBlock:
         step = self.attn_chunk or s
         if step >= s:
             o = F.scaled_dot_product_attention(qh, kh, vh).transpose(1, 2).reshape(s, inner)
-        else:  # query rows are independent: chunking is exact
+        else:  # query rows are independent (chunks may pick another attention kernel: not bit-identical)
             o = torch.empty(s, inner, dtype=h.dtype, device=h.device)
             for a in range(0, s, step):
                 o[a:a + step] = F.scaled_dot_product_attention(qh[:, :, a:a + step], kh, vh)[0].transpose(0, 1).reshape(-1, inner)

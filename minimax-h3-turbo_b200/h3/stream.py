@@ -117,6 +117,7 @@ class StreamingProvider:
         self._stop = self._closed = self._in_forward = False
         self._error: Optional[BaseException] = None
         self._thread: Optional[threading.Thread] = None
+        self._inline = False  # copies issued by the caller's thread (see _start_worker)
         self._engine: Optional[int] = None
         self._n_staging = 0
         self._st = dict(acquires=0, waits=0, wait_s=0.0, copies=0, bytes=0, busy_s=0.0)
@@ -176,10 +177,12 @@ class StreamingProvider:
             self._start_worker()
 
     def _register(self, t: torch.Tensor, read_only: bool) -> bool:
-        rc = _lib.lib().h3b_host_register(t.data_ptr(), t.numel(), int(read_only))
+        L = _lib.lib()
+        rc = L.h3b_host_register(t.data_ptr(), t.numel(), int(read_only))
         if rc == 0:
             self._reg_ptrs.append(t.data_ptr())
             return True
+        self._plan_info["register_error" if read_only else "pin_error"] = (L.h3b_last_error() or b"").decode(errors="replace")
         return False
 
     def _plan_host(self, pin, pin_mode, pin_fraction, headroom, pin_blocks) -> None:
@@ -226,8 +229,38 @@ class StreamingProvider:
 
     # ------------------------------------------------------------------ worker
     def _start_worker(self) -> None:
+        """Copies from pinned or registered host memory only enqueue work (a device-side wait, cudaMemcpyAsync, an event
+        record), so they are issued inline by the thread that calls acquire/release ("inline" mode): no worker thread
+        has to win the interpreter lock from a busy model thread before a copy starts.  Staged and pageable copies
+        block the host, and test hooks may sleep, so those run on the worker thread (stream.py:305-331)."""
+        self._inline = (self._cuda and self._transfer is None and bool(self._streamed)
+                        and all(self._kind.get(b) in ("registered", "pinned") for b in self._streamed))
+        self._plan_info["issue"] = "inline" if self._inline else "worker"
+        if self._inline:
+            self._pump()
+            return
         self._thread = threading.Thread(target=self._run, name="h3b-stream", daemon=True)
         self._thread.start()
+
+    def _pump(self) -> None:
+        """Inline mode: issue every copy the lookahead window allows, on the calling thread."""
+        if not self._inline:
+            return
+        while True:
+            with self._cv:
+                if self._closed or self._error is not None:
+                    return
+                job = self._next_job()
+            if job is None:
+                return
+            try:
+                self._issue(*job)
+            except BaseException as e:
+                with self._cv:
+                    self._error = e
+                raise
+            with self._cv:
+                job[0].state = READY
 
     def _targets(self) -> List[int]:
         S = self._streamed
@@ -336,6 +369,14 @@ class StreamingProvider:
         t0 = time.perf_counter()
         deadline = t0 + self._timeout
         waited = False
+        if self._inline:
+            with self._cv:
+                self._check()
+                if i not in self._by_block:
+                    if all(s.state == ACQUIRED for s in self._slots):
+                        raise RuntimeError(f"all {len(self._slots)} ring slots are held; release() a block before acquiring block {i} (ring too small?)")
+                    self._demand = i
+            self._pump()
         with self._cv:
             self._check()
             while True:
@@ -368,6 +409,7 @@ class StreamingProvider:
             self._cv.notify_all()  # the lookahead window moved
         if self._cuda:
             _lib.check(_lib.lib().h3b_streamer_acquire(self._engine, slot.idx, _lib.stream_ptr(self.device)), "streamer acquire")
+        self._pump()
         return slot.weights
 
     def release(self, i: int) -> None:
@@ -383,6 +425,7 @@ class StreamingProvider:
             self._tick += 1
             slot.stamp = self._tick
             self._cv.notify_all()
+        self._pump()
 
     def end_forward(self) -> None:
         """Reset for the next forward (safe after an exception): held slots are released behind the current stream and
@@ -395,6 +438,8 @@ class StreamingProvider:
                     s.state = IDLE
             self._pos, self._demand, self._in_forward = -1, None, False
             self._cv.notify_all()
+        if not self._closed:
+            self._pump()
 
     # ------------------------------------------------------------------ residency changes (between forwards)
     def device_bytes(self) -> int:
@@ -432,6 +477,7 @@ class StreamingProvider:
         if self._in_forward:
             raise RuntimeError("resize() during a forward")
         self._stop_worker()
+        self._inline = False
         if self._cuda:
             torch.cuda.synchronize(self.device)
         n = self.n_blocks
@@ -498,6 +544,7 @@ class StreamingProvider:
     def wait_prefetch(self, timeout: float = 60.0) -> None:
         """Block until the worker has nothing left to issue and every issued copy has landed."""
         deadline = time.perf_counter() + timeout
+        self._pump()
         with self._cv:
             while self._thread is not None and not self._stop and self._error is None and (
                     any(s.state == PENDING for s in self._slots) or self._next_job(commit=False) is not None):

@@ -1,5 +1,5 @@
 """The DiT block on the W4A8 kernels (GPU): against the same block in fp32 on the dequantized weights (the difference is
-the int8 activation quantisation noise, ~1 %), exact query chunking, and the block fed by the streaming provider."""
+the int8 activation quantisation noise, ~1 % per linear), query chunking, and the block fed by the streaming provider."""
 import pytest
 import torch
 
@@ -27,12 +27,10 @@ def make(seed=0):
     return x, w, mod, [(0, 270, 0), (270, S, 1)], cos, sin
 
 
-def test_block_matches_the_dequantized_fp32_block():
-    x, w, mod, seg, cos, sin = make()
-    y = blk.DiTBlock(HEADS, HD)(x.clone(), w, mod, seg, cos, sin)
+def _dense_reference(w):
+    """The same block in fp32 on the dequantized weights (original basis) with a plain dense linear."""
     dense = {k: ql.dequantize(getattr(w, k), torch.float32) for k in ("qkv", "out", "fc1", "fc2")}
-    wd = BlockWeights(qkv=dense["qkv"], out=dense["out"], fc1=dense["fc1"], fc2=dense["fc2"], norm1=w.norm1.float(),
-                      norm2=w.norm2.float(), q_norm=w.q_norm.float(), k_norm=w.k_norm.float())
+    wd = BlockWeights(**dense, norm1=w.norm1.float(), norm2=w.norm2.float(), q_norm=w.q_norm.float(), k_norm=w.k_norm.float())
 
     def lin(t, wt, input_act=None):
         if input_act == "swiglu":
@@ -40,17 +38,43 @@ def test_block_matches_the_dequantized_fp32_block():
             t = torch.nn.functional.silu(g) * u
         return t @ wt.t()
 
-    ref = blk.DiTBlock(HEADS, HD, linear=lin)(x.float(), wd, mod, seg, cos.float(), sin.float())
-    upd, ref_upd = (y.float() - x.float()), (ref - x.float())
-    rel = (upd - ref_upd).norm() / ref_upd.norm()
-    assert torch.isfinite(y.float()).all() and rel < 0.05, rel.item()
+    return blk.DiTBlock(HEADS, HD, linear=lin), wd
 
 
-def test_chunked_attention_is_exact():
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+def test_attention_and_mlp_branches_match_the_dequantized_fp32_block():
+    """The W4A8 branches differ from fp32 on the dequantized weights only by the int8 activation quantisation (~1 %
+    per linear, outlier channels spread by the rotation) and bf16 intermediates."""
+    x, w, mod, seg, cos, sin = make()
+    ref_block, wd = _dense_reference(w)
+    h = blk.rms(x, w.norm1, 1e-5)
+    a = blk.DiTBlock(HEADS, HD).attention(h.clone(), w, cos, sin)
+    a_ref = ref_block.attention(h.float(), wd, cos.float(), sin.float())
+    m = blk.DiTBlock(HEADS, HD).mlp(h.clone(), w)
+    m_ref = ref_block.mlp(h.float(), wd)
+    assert _rel(a, a_ref) < 0.05 and _rel(m, m_ref) < 0.05, (_rel(a, a_ref), _rel(m, m_ref))
+
+
+def test_block_matches_the_dequantized_fp32_block():
+    x, w, _, seg, cos, sin = make()
+    g = torch.Generator(device=DEV).manual_seed(9)
+    mod = blk.Modulation(*(torch.randn(2, HID, generator=g, device=DEV) for _ in range(6)))  # unit-scale gates
+    y = blk.DiTBlock(HEADS, HD)(x.clone(), w, mod, seg, cos, sin)
+    ref_block, wd = _dense_reference(w)
+    ref = ref_block(x.float(), wd, mod, seg, cos.float(), sin.float())
+    assert torch.isfinite(y.float()).all()
+    assert _rel(y.float() - x.float(), ref - x.float()) < 0.05
+
+
+def test_chunked_attention_matches():
+    """Query rows are independent, so chunking changes only which attention kernel runs and its summation order."""
     x, w, mod, seg, cos, sin = make(1)
     a = blk.DiTBlock(HEADS, HD)(x.clone(), w, mod, seg, cos, sin)
     b = blk.DiTBlock(HEADS, HD, attn_chunk=64)(x.clone(), w, mod, seg, cos, sin)
-    assert torch.equal(a, b)
+    assert _rel(a - x, b - x) < 1e-2
 
 
 def test_single_rank_shard_spec_is_a_no_op():

@@ -43,6 +43,8 @@ def test_device_bytes_equal_the_file_in_every_host_mode(store, pin, pin_mode):
                 p.release(i)
             p.end_forward()
         kinds = p.stats()["host_kinds"]
+        issue = p.stats()["plan"]["issue"]
+    assert issue == ("inline" if set(kinds) <= {"registered", "pinned"} else "worker"), (kinds, issue)
     if pin is False:
         assert set(kinds) == {"pageable"}
     elif pin_mode == "stage":
