@@ -68,6 +68,17 @@ int h3b_rotq(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int 
 int h3b_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int convrot, void* y, int y_dtype,
                int64_t ldy, void* stream);
 
+/* Per-head RMSNorm + split-half rotary embedding of q and k, in place (both, or one of them with the other NULL).
+ * Replaces comfy_kitchen's rms_rope_split_half_ (called at layout.py:343) with the bit-exact semantics of the
+ * reference's "torch" form of that kernel, norm_rope_ (layout.py:329-356) with rms_norm_fused_order (layout.py:309-326).
+ *   q, k      [S, heads, head_dim] of x_dtype (bf16 or fp16), heads contiguous, token strides ldq / ldk (elements);
+ *             head_dim 32, 64, 128 or 256
+ *   wq, wk    [head_dim] of w_dtype;  eps as the fp32 value of the model's qk_norm_eps
+ *   cos, sin  [S, half] of t_dtype, rows ldt elements apart; channel j < half pairs with j + half; 2 * half <= head_dim */
+int h3b_qk_norm_rope(void* q, int64_t ldq, void* k, int64_t ldk, int x_dtype, int64_t S, int heads, int head_dim,
+                     const void* wq, const void* wk, int w_dtype, float eps, const void* cos_t, const void* sin_t,
+                     int64_t ldt, int t_dtype, int half, void* stream);
+
 /* int4 codebook indices + group scales -> the exact int8 grid [N, K] (row stride ldg bytes).
  * Replaces decode_int8_grid / _decode_rows / _pair_lut (qlinear.py:157-204).
  *   q4     [N, ldq4 bytes] packed nibbles, low nibble first (types.py:14-16)

@@ -29,6 +29,7 @@ int check_launch(const char* what) {
 
 #include "decode.cuh"
 #include "gemm_sm100.cuh"
+#include "rope.cuh"
 #include "rotq.cuh"
 #include "streamer.cuh"
 
@@ -139,6 +140,22 @@ int h3b_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, in
   if (M == 0) return H3B_OK;
   return rotq_launch(x, x_dtype, M, K, ldx, convrot, 0, MODE_ROTATE, nullptr, 0, nullptr, y, y_dtype, ldy,
                      static_cast<cudaStream_t>(stream));
+}
+
+int h3b_qk_norm_rope(void* q, int64_t ldq, void* k, int64_t ldk, int x_dtype, int64_t S, int heads, int head_dim,
+                     const void* wq, const void* wk, int w_dtype, float eps, const void* cos_t, const void* sin_t,
+                     int64_t ldt, int t_dtype, int half, void* stream) {
+  if (S == 0) return H3B_OK;  // empty sequence (torch hands out null pointers for empty tensors)
+  if (!q && !k) return fail(H3B_ERR_ARG, "qk_norm_rope: q and k are both null");
+  if ((q && !wq) || (k && !wk)) return fail(H3B_ERR_ARG, "qk_norm_rope: a norm weight is missing");
+  if (S < 0 || heads < 1 || head_dim < 1) return fail(H3B_ERR_ARG, "qk_norm_rope: bad shape");
+  if ((q && ldq < static_cast<int64_t>(heads) * head_dim) || (k && ldk < static_cast<int64_t>(heads) * head_dim))
+    return fail(H3B_ERR_ARG, "qk_norm_rope: token stride is smaller than heads * head_dim");
+  if (!is_act(w_dtype) || !is_act(t_dtype)) return fail(H3B_ERR_ARG, "qk_norm_rope: weight/table dtype must be bf16, fp16 or fp32");
+  if (half < 0 || 2 * half > head_dim) return fail(H3B_ERR_ARG, "qk_norm_rope: 2 * half exceeds head_dim");
+  if (half > 0 && (!cos_t || !sin_t || ldt < half)) return fail(H3B_ERR_ARG, "qk_norm_rope: cos/sin tables missing or too narrow");
+  return qk_norm_rope_launch(q, ldq, k, ldk, x_dtype, S, heads, head_dim, wq, wk, w_dtype, eps, cos_t, sin_t, ldt, t_dtype,
+                             half, static_cast<cudaStream_t>(stream));
 }
 
 int h3b_decode_grid(const void* q4, int64_t N, int64_t K, int64_t ldq4, const void* s_rel, int s_dtype, int64_t lds,

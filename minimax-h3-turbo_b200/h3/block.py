@@ -10,8 +10,8 @@ _rms / _scale_shift_ / _gate_ :64-115 and q/k norm + split-half RoPE, layout.py:
     h = rms(x, norm2) * (1 + sc_m) + sh_m
     x = x + g_m * qlinear(qlinear(h, fc1), fc2, input_act="swiglu")
 
-Every linear is the W4A8 qlinear (kernels KA + KB); norms, RoPE, modulation and attention are torch ops (attention
-through torch's SDPA, i.e. the flash / cuDNN library kernels, bf16).
+Every linear is the W4A8 qlinear (kernels KA + KB); q/k norm + RoPE is the fused kernel of `rope.norm_rope_`; the
+other norms, the modulation and attention are torch ops (attention through torch's SDPA library kernels, bf16).
 
 Token sharding (rank r of P owns a contiguous slice of rows): every op above is token-wise except attention, which needs
 all keys and values; each block therefore all-gathers K and V (bf16, [S_local, inner] each) over NCCL before the local
@@ -26,6 +26,7 @@ import torch
 import torch.nn.functional as F
 
 from . import qlinear as ql
+from .rope import norm_rope_
 from .types import BlockWeights
 
 Segment = Tuple[int, int, int]  # (first row, end row, modulation row)
@@ -34,36 +35,6 @@ Segment = Tuple[int, int, int]  # (first row, end row, modulation row)
 def rms(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """F.rms_norm over the last dim with the weight in x.dtype (model.py:64-66)."""
     return F.rms_norm(x, (x.shape[-1],), weight if weight.dtype == x.dtype else weight.to(x.dtype), eps)
-
-
-def rms_lane_order(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """Per-head RMSNorm with the fused kernel's summation order (layout.py:309-326): lane l sums the squares of
-    elements l, l + 32, ... in fp32, then a halving tree over the 32 lanes; x * rsqrt(sum / d + eps) * w rounded once."""
-    d = x.shape[-1]
-    if x.dtype == torch.float32 or d % 32:
-        return F.rms_norm(x, (d,), weight.to(x.dtype), eps)
-    xf = x.to(torch.float32)
-    sq = xf.square().reshape(*x.shape[:-1], d // 32, 32)
-    acc = sq[..., 0, :]
-    for j in range(1, d // 32):
-        acc = acc + sq[..., j, :]
-    for off in (16, 8, 4, 2, 1):
-        acc = acc[..., :off] + acc[..., off:2 * off]
-    return (xf * torch.rsqrt(acc / d + eps) * weight.to(torch.float32)).to(x.dtype)
-
-
-def norm_rope_(x: torch.Tensor, w: torch.Tensor, eps: float, cos: torch.Tensor, sin: torch.Tensor, chunk: int = 4096) -> None:
-    """In place on a [S, heads, D] view: per-head RMSNorm, then the split-half rotation of the first 2 * half channels
-    (angle j pairs channel j with channel j + half), rotation in fp32, rounded once."""
-    half = cos.shape[1]
-    for a in range(0, x.shape[0], chunk):
-        sl = slice(a, a + chunk)
-        xn = rms_lane_order(x[sl], w, eps)
-        c, s = cos[sl].unsqueeze(1).to(torch.float32), sin[sl].unsqueeze(1).to(torch.float32)
-        x1, x2 = xn[..., :half].to(torch.float32), xn[..., half:2 * half].to(torch.float32)
-        o1, o2 = x1 * c - x2 * s, x1 * s + x2 * c
-        xn[..., :half], xn[..., half:2 * half] = o1, o2
-        x[sl] = xn
 
 
 def scale_shift_(h: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, segments: Sequence[Segment]) -> torch.Tensor:
@@ -148,8 +119,7 @@ class DiTBlock:
         inner = heads * hd
         qkv = self._linear(h, w.qkv)
         q, k, v = (t.view(s, heads, hd) for t in qkv.split(inner, dim=-1))
-        norm_rope_(q, w.q_norm, self.qk_norm_eps, cos, sin)
-        norm_rope_(k, w.k_norm, self.qk_norm_eps, cos, sin)
+        norm_rope_(q, k, w.q_norm, w.k_norm, self.qk_norm_eps, cos, sin)
         if spec is not None and spec.world > 1:  # every query needs every key and value
             k = gather_rows(k.reshape(s, inner).contiguous(), spec).view(-1, heads, hd)
             v = gather_rows(v.reshape(s, inner).contiguous(), spec).view(-1, heads, hd)

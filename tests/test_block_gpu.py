@@ -72,9 +72,10 @@ def test_block_matches_the_dequantized_fp32_block():
 def test_chunked_attention_matches():
     """Query rows are independent, so chunking changes only which attention kernel runs and its summation order."""
     x, w, mod, seg, cos, sin = make(1)
-    a = blk.DiTBlock(HEADS, HD)(x.clone(), w, mod, seg, cos, sin)
-    b = blk.DiTBlock(HEADS, HD, attn_chunk=64)(x.clone(), w, mod, seg, cos, sin)
-    assert _rel(a - x, b - x) < 1e-2
+    h = blk.rms(x, w.norm1, 1e-5)
+    a = blk.DiTBlock(HEADS, HD).attention(h.clone(), w, cos, sin)
+    b = blk.DiTBlock(HEADS, HD, attn_chunk=64).attention(h.clone(), w, cos, sin)
+    assert _rel(b, a) < 1e-2
 
 
 def test_single_rank_shard_spec_is_a_no_op():
