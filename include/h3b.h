@@ -79,6 +79,29 @@ int h3b_qk_norm_rope(void* q, int64_t ldq, void* k, int64_t ldk, int x_dtype, in
                      const void* wq, const void* wk, int w_dtype, float eps, const void* cos_t, const void* sin_t,
                      int64_t ldt, int t_dtype, int half, void* stream);
 
+/* RMSNorm + AdaLN modulation of the residual stream: h = scale_shift(rms(x)).  Replaces _rms followed by _scale_shift_
+ * (model.py:64-66, 106-109): n = dt((x * rsqrt(mean(x^2) + eps)) * w), then for a token with modulation row `row`
+ * h = dt(dt(n * dt(1 + dt(scale[row]))) + dt(shift[row])); tokens without a row keep n.  The row sum's order is this
+ * kernel's own (torch's F.rms_norm reduces in another order: rare one-ulp differences of n).
+ *   x, h          [M, hidden] of x_dtype (bf16 or fp16), rows ldx / ldh elements apart; hidden a multiple of 8
+ *   w             [hidden] of w_dtype;  shift, scale: [n_rows, hidden] of m_dtype, rows ldm elements apart
+ *   segments      HOST table of n_segments <= H3B_MAX_SEGMENTS x (first token, end token, row), int32
+ *   token_rows    optional DEVICE int32 [M] row per token (negative: none, else < n_rows, which the caller guarantees);
+ *                 used instead of the segments when given
+ *   every device pointer 16-byte aligned */
+#define H3B_MAX_SEGMENTS 16
+int h3b_rms_modulate(const void* x, int x_dtype, int64_t ldx, int64_t M, int hidden, const void* w, int w_dtype,
+                     float eps, const void* shift, const void* scale, int64_t ldm, int64_t n_rows, int m_dtype,
+                     const int32_t* segments, int n_segments, const int32_t* token_rows, void* h, int64_t ldh,
+                     void* stream);
+
+/* Gated residual update, in place: x = dt(x + other * dt(gate[row])) for tokens with a modulation row, others
+ * unchanged.  Replaces _gate_ (model.py:111-115; torch's addcmul_, bit-identical).  Arguments as h3b_rms_modulate;
+ * other: [M, hidden] of x_dtype, rows ldo elements apart. */
+int h3b_gate_residual(void* x, int x_dtype, int64_t ldx, const void* other, int64_t ldo, int64_t M, int hidden,
+                      const void* gate, int64_t ldm, int64_t n_rows, int m_dtype, const int32_t* segments, int n_segments,
+                      const int32_t* token_rows, void* stream);
+
 /* int4 codebook indices + group scales -> the exact int8 grid [N, K] (row stride ldg bytes).
  * Replaces decode_int8_grid / _decode_rows / _pair_lut (qlinear.py:157-204).
  *   q4     [N, ldq4 bytes] packed nibbles, low nibble first (types.py:14-16)

@@ -39,6 +39,10 @@ _SIGNATURES = {
     "h3b_rotate": ([_c_void_p, _int, _i64, _i64, _i64, _int, _c_void_p, _int, _i64, _c_void_p], _int),
     "h3b_qk_norm_rope": ([_c_void_p, _i64, _c_void_p, _i64, _int, _i64, _int, _int, _c_void_p, _c_void_p, _int,
                           ctypes.c_float, _c_void_p, _c_void_p, _i64, _int, _int, _c_void_p], _int),
+    "h3b_rms_modulate": ([_c_void_p, _int, _i64, _i64, _int, _c_void_p, _int, ctypes.c_float, _c_void_p, _c_void_p, _i64,
+                          _i64, _int, _c_void_p, _int, _c_void_p, _c_void_p, _i64, _c_void_p], _int),
+    "h3b_gate_residual": ([_c_void_p, _int, _i64, _c_void_p, _i64, _i64, _int, _c_void_p, _i64, _i64, _int, _c_void_p, _int,
+                           _c_void_p, _c_void_p], _int),
     "h3b_decode_grid": ([_c_void_p, _i64, _i64, _i64, _c_void_p, _int, _i64, _c_void_p, _int, _c_void_p, _i64, _c_void_p], _int),
     "h3b_int8_gemm_s32": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p], _int),
     "h3b_gemm_workspace_bytes": ([_i64, _i64, _i64], _sz),

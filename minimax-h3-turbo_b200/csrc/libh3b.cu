@@ -29,6 +29,7 @@ int check_launch(const char* what) {
 
 #include "decode.cuh"
 #include "gemm_sm100.cuh"
+#include "rmsmod.cuh"
 #include "rope.cuh"
 #include "rotq.cuh"
 #include "streamer.cuh"
@@ -156,6 +157,49 @@ int h3b_qk_norm_rope(void* q, int64_t ldq, void* k, int64_t ldk, int x_dtype, in
   if (half > 0 && (!cos_t || !sin_t || ldt < half)) return fail(H3B_ERR_ARG, "qk_norm_rope: cos/sin tables missing or too narrow");
   return qk_norm_rope_launch(q, ldq, k, ldk, x_dtype, S, heads, head_dim, wq, wk, w_dtype, eps, cos_t, sin_t, ldt, t_dtype,
                              half, static_cast<cudaStream_t>(stream));
+}
+
+int h3b_rms_modulate(const void* x, int x_dtype, int64_t ldx, int64_t M, int hidden, const void* w, int w_dtype,
+                     float eps, const void* shift, const void* scale, int64_t ldm, int64_t n_rows, int m_dtype,
+                     const int32_t* segments, int n_segments, const int32_t* token_rows, void* h, int64_t ldh,
+                     void* stream) {
+  if (M < 0 || hidden < 8 || hidden % 8) return fail(H3B_ERR_ARG, "rms_modulate: hidden must be a positive multiple of 8");
+  if (M == 0) return H3B_OK;
+  if (!x || !w || !h) return fail(H3B_ERR_ARG, "rms_modulate: null x, weight or output");
+  if (ldx < hidden || ldh < hidden || ldx % 8 || ldh % 8 || !aligned(x, 16) || !aligned(h, 16) || !aligned(w, 16))
+    return fail(H3B_ERR_ARG, "rms_modulate: x / h / weight must be 16-byte aligned with row strides >= hidden, multiples of 8");
+  if (n_segments < 0 || n_segments > H3B_MAX_SEGMENTS || (n_segments > 0 && !segments))
+    return fail(H3B_ERR_ARG, "rms_modulate: at most H3B_MAX_SEGMENTS segments, given as a host table");
+  const bool mod = n_segments > 0 || token_rows;
+  if (!is_act(w_dtype) || (mod && !is_act(m_dtype))) return fail(H3B_ERR_ARG, "rms_modulate: bad weight / modulation dtype");
+  if (mod && (!shift || !scale || ldm < hidden || ldm % 8 || !aligned(shift, 16) || !aligned(scale, 16)))
+    return fail(H3B_ERR_ARG, "rms_modulate: shift/scale must be 16-byte aligned rows of >= hidden, stride a multiple of 8");
+  for (int i = 0; i < n_segments; ++i)
+    if (segments[3 * i] < 0 || segments[3 * i + 1] < segments[3 * i] || segments[3 * i + 2] < 0 ||
+        segments[3 * i + 2] >= n_rows)
+      return fail(H3B_ERR_ARG, "rms_modulate: a segment has a negative bound, ends before it starts, or names a row >= n_rows");
+  return rms_modulate_launch(x, x_dtype, ldx, M, hidden, w, w_dtype, eps, shift, scale, ldm, m_dtype, segments, n_segments,
+                             token_rows, h, ldh, static_cast<cudaStream_t>(stream));
+}
+
+int h3b_gate_residual(void* x, int x_dtype, int64_t ldx, const void* other, int64_t ldo, int64_t M, int hidden,
+                      const void* gate, int64_t ldm, int64_t n_rows, int m_dtype, const int32_t* segments, int n_segments,
+                      const int32_t* token_rows, void* stream) {
+  if (M < 0 || hidden < 8 || hidden % 8) return fail(H3B_ERR_ARG, "gate_residual: hidden must be a positive multiple of 8");
+  if (M == 0 || (n_segments == 0 && !token_rows)) return H3B_OK;
+  if (!x || !other || !gate) return fail(H3B_ERR_ARG, "gate_residual: null x, other or gate");
+  if (ldx < hidden || ldo < hidden || ldm < hidden || ldx % 8 || ldo % 8 || ldm % 8 || !aligned(x, 16) ||
+      !aligned(other, 16) || !aligned(gate, 16))
+    return fail(H3B_ERR_ARG, "gate_residual: 16-byte aligned rows with strides >= hidden, multiples of 8, are required");
+  if (!is_act(m_dtype)) return fail(H3B_ERR_ARG, "gate_residual: bad gate dtype");
+  if (n_segments < 0 || n_segments > H3B_MAX_SEGMENTS || (n_segments > 0 && !segments))
+    return fail(H3B_ERR_ARG, "gate_residual: at most H3B_MAX_SEGMENTS segments, given as a host table");
+  for (int i = 0; i < n_segments; ++i)
+    if (segments[3 * i] < 0 || segments[3 * i + 1] < segments[3 * i] || segments[3 * i + 2] < 0 ||
+        segments[3 * i + 2] >= n_rows)
+      return fail(H3B_ERR_ARG, "gate_residual: a segment has a negative bound, ends before it starts, or names a row >= n_rows");
+  return gate_residual_launch(x, x_dtype, ldx, other, ldo, M, hidden, gate, ldm, m_dtype, segments, n_segments, token_rows,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int h3b_decode_grid(const void* q4, int64_t N, int64_t K, int64_t ldq4, const void* s_rel, int s_dtype, int64_t lds,

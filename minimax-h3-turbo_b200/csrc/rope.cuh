@@ -39,17 +39,18 @@ __device__ __forceinline__ float ld_any(const void* p, int64_t i, int dt) {
 
 constexpr int ROPE_WARPS = 8;
 
-// NI = D / 32 channels per lane.  Items: (token, head) of q, then of k.
-template <int DT, int NI>
+// NI = D / 32 channels per lane; HPI heads of one token per warp item (their loads are issued together).
+// Items: (token, head group) of q, then of k.
+template <int DT, int NI, int HPI>
 __global__ void __launch_bounds__(32 * ROPE_WARPS) qk_norm_rope_kernel(
     void* __restrict__ q, int64_t ldq, void* __restrict__ k, int64_t ldk, int64_t S, int heads,
     const void* __restrict__ wq, const void* __restrict__ wk, int w_dtype, float eps, const void* __restrict__ cs,
     const void* __restrict__ sn, int64_t ldt, int t_dtype, int half) {
   constexpr int D = 32 * NI;
-  __shared__ float stage[ROPE_WARPS][D];
+  __shared__ float stage[ROPE_WARPS][HPI][D];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  float* row = stage[wid];
-  const int64_t per = S * heads;
+  const int groups = heads / HPI;
+  const int64_t per = S * groups;
   const int64_t items = (q ? per : 0) + (k ? per : 0);
   const float inv_d = 1.0f / static_cast<float>(D);  // exact: D is a power of two
   float wv[2][NI];
@@ -62,41 +63,55 @@ __global__ void __launch_bounds__(32 * ROPE_WARPS) qk_norm_rope_kernel(
        it += static_cast<int64_t>(gridDim.x) * ROPE_WARPS) {
     const bool is_k = !q || it >= per;
     const int64_t r = (q && it >= per) ? it - per : it;
-    const int64_t tok = r / heads, h = r - tok * heads;
+    const int64_t tok = r / groups, h0 = (r - tok * groups) * HPI;
     void* base = is_k ? k : q;
-    const int64_t off = tok * (is_k ? ldk : ldq) + h * D;
-    float x[NI];
+    const int64_t off = tok * (is_k ? ldk : ldq) + h0 * D;
+    float x[HPI][NI];
 #pragma unroll
-    for (int i = 0; i < NI; ++i) x[i] = ld_act<DT>(base, off + lane + 32 * i);
-    float acc = __fmul_rn(x[0], x[0]);
+    for (int hh = 0; hh < HPI; ++hh)
 #pragma unroll
-    for (int i = 1; i < NI; ++i) acc = __fadd_rn(acc, __fmul_rn(x[i], x[i]));
+      for (int i = 0; i < NI; ++i) x[hh][i] = ld_act<DT>(base, off + hh * D + lane + 32 * i);
+    float acc[HPI];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, o));
-    acc = __shfl_sync(0xffffffffu, acc, 0);
-    const float rs = rsqrtf(__fadd_rn(__fmul_rn(acc, inv_d), eps));
-    float n[NI];
+    for (int hh = 0; hh < HPI; ++hh) {
+      acc[hh] = __fmul_rn(x[hh][0], x[hh][0]);
 #pragma unroll
-    for (int i = 0; i < NI; ++i) {
-      n[i] = rnd_act<DT>(__fmul_rn(__fmul_rn(x[i], rs), is_k ? wv[1][i] : wv[0][i]));
-      row[lane + 32 * i] = n[i];
+      for (int i = 1; i < NI; ++i) acc[hh] = __fadd_rn(acc[hh], __fmul_rn(x[hh][i], x[hh][i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int hh = 0; hh < HPI; ++hh) acc[hh] = __fadd_rn(acc[hh], __shfl_down_sync(0xffffffffu, acc[hh], o));
+    float n[HPI][NI];
+#pragma unroll
+    for (int hh = 0; hh < HPI; ++hh) {
+      const float rs = rsqrtf(__fadd_rn(__fmul_rn(__shfl_sync(0xffffffffu, acc[hh], 0), inv_d), eps));
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        n[hh][i] = rnd_act<DT>(__fmul_rn(__fmul_rn(x[hh][i], rs), is_k ? wv[1][i] : wv[0][i]));
+        stage[wid][hh][lane + 32 * i] = n[hh][i];
+      }
     }
     __syncwarp();
     const int64_t trow = tok * ldt;
 #pragma unroll
     for (int i = 0; i < NI; ++i) {
       const int c = lane + 32 * i;
-      float o = n[i];
-      if (c < half) {
-        const float cv = ld_any(cs, trow + c, t_dtype), sv = ld_any(sn, trow + c, t_dtype);
-        o = __fsub_rn(__fmul_rn(n[i], cv), __fmul_rn(row[c + half], sv));
-      } else if (c < 2 * half) {
-        const float cv = ld_any(cs, trow + c - half, t_dtype), sv = ld_any(sn, trow + c - half, t_dtype);
-        o = __fadd_rn(__fmul_rn(row[c - half], sv), __fmul_rn(n[i], cv));
+      float cv = 0.f, sv = 0.f;
+      if (c < 2 * half) {
+        const int j = c < half ? c : c - half;
+        cv = ld_any(cs, trow + j, t_dtype);
+        sv = ld_any(sn, trow + j, t_dtype);
       }
-      st_act<DT>(base, off + c, o);
+#pragma unroll
+      for (int hh = 0; hh < HPI; ++hh) {
+        float o = n[hh][i];
+        if (c < half) o = __fsub_rn(__fmul_rn(n[hh][i], cv), __fmul_rn(stage[wid][hh][c + half], sv));
+        else if (c < 2 * half) o = __fadd_rn(__fmul_rn(stage[wid][hh][c - half], sv), __fmul_rn(n[hh][i], cv));
+        st_act<DT>(base, off + hh * D + c, o);
+      }
     }
-    __syncwarp();  // the next item overwrites this warp's staging row
+    __syncwarp();  // the next item overwrites this warp's staging rows
   }
 }
 
@@ -107,17 +122,22 @@ static int qk_launch_d(void* q, int64_t ldq, void* k, int64_t ldk, int64_t S, in
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t items = S * heads * ((q ? 1 : 0) + (k ? 1 : 0));
+  const int hpi = heads % 4 == 0 && D <= 128 ? 4 : heads % 2 == 0 ? 2 : 1;
+  const int64_t items = S * (heads / hpi) * ((q ? 1 : 0) + (k ? 1 : 0));
   const int64_t want = (items + ROPE_WARPS - 1) / ROPE_WARPS;
   const int64_t cap = static_cast<int64_t>(sms) * 8;  // 8 resident 256-thread CTAs per SM
   const int blocks = static_cast<int>(want < cap ? want : cap);
+#define H3B_QKR(NI, HPI) qk_norm_rope_kernel<DT, NI, HPI><<<blocks, 32 * ROPE_WARPS, 0, st>>>(q, ldq, k, ldk, S, heads, wq, wk, w_dtype, eps, cs, sn, ldt, t_dtype, half)
+#define H3B_QKR_H(NI) if (hpi == 4) H3B_QKR(NI, 4); else if (hpi == 2) H3B_QKR(NI, 2); else H3B_QKR(NI, 1)
   switch (D) {
-    case 32: qk_norm_rope_kernel<DT, 1><<<blocks, 32 * ROPE_WARPS, 0, st>>>(q, ldq, k, ldk, S, heads, wq, wk, w_dtype, eps, cs, sn, ldt, t_dtype, half); break;
-    case 64: qk_norm_rope_kernel<DT, 2><<<blocks, 32 * ROPE_WARPS, 0, st>>>(q, ldq, k, ldk, S, heads, wq, wk, w_dtype, eps, cs, sn, ldt, t_dtype, half); break;
-    case 128: qk_norm_rope_kernel<DT, 4><<<blocks, 32 * ROPE_WARPS, 0, st>>>(q, ldq, k, ldk, S, heads, wq, wk, w_dtype, eps, cs, sn, ldt, t_dtype, half); break;
-    case 256: qk_norm_rope_kernel<DT, 8><<<blocks, 32 * ROPE_WARPS, 0, st>>>(q, ldq, k, ldk, S, heads, wq, wk, w_dtype, eps, cs, sn, ldt, t_dtype, half); break;
+    case 32: H3B_QKR_H(1); break;
+    case 64: H3B_QKR_H(2); break;
+    case 128: H3B_QKR_H(4); break;
+    case 256: if (hpi == 1) H3B_QKR(8, 1); else H3B_QKR(8, 2); break;
     default: return fail(H3B_ERR_UNSUPPORTED, "qk_norm_rope: head_dim must be 32, 64, 128 or 256");
   }
+#undef H3B_QKR_H
+#undef H3B_QKR
   return check_launch("qk_norm_rope_kernel");
 }
 

@@ -44,7 +44,76 @@ def scale_shift_(h: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, segm
     return h
 
 
+def _aligned_rows(t: torch.Tensor) -> torch.Tensor:
+    """t itself when it is a row-major 2-D view the kernels can read (16-byte aligned, row stride a multiple of 8)."""
+    ok = t.dim() == 2 and t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
+    return t if ok else t.contiguous()
+
+
+def _segment_args(segments: Sequence[Segment], m: int, n_rows: int, device):
+    """(host int32 table or None, its length, device per-token row map or None) for the modulation kernels: up to 16
+    segments with int rows go by value; more, or per-token row tensors (the reference's _pieces), use a row map."""
+    import ctypes
+
+    segs = [(a, b, r) for a, b, r in segments if b > a]
+    if len(segs) <= 16 and all(isinstance(r, int) for _, _, r in segs):
+        for a, b, r in segs:
+            if not 0 <= r < n_rows or a < 0 or b > m:
+                raise ValueError(f"segment {(a, b, r)} is out of range for {m} tokens and {n_rows} modulation rows")
+        return (ctypes.c_int32 * max(1, 3 * len(segs)))(*[v for seg in segs for v in seg]), len(segs), None
+    rows = torch.full((m,), -1, dtype=torch.int32, device=device)
+    for a, b, r in segs:
+        rows[a:b] = r.to(device=device, dtype=torch.int32) if isinstance(r, torch.Tensor) else int(r)
+    return None, 0, rows
+
+
+def _kernel_rows(x: torch.Tensor) -> bool:
+    return x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and x.dim() == 2 and x.shape[1] % 8 == 0
+
+
+def rms_modulate(x: torch.Tensor, weight: torch.Tensor, eps: float, shift: torch.Tensor, scale: torch.Tensor,
+                 segments: Sequence[Segment]) -> torch.Tensor:
+    """h = scale_shift_(rms(x, weight, eps), shift, scale, segments) as one pass over x (model.py:64-66, 106-109) on the
+    fused kernel for bf16/fp16 CUDA tensors (rows: ints, or int tensors of per-token rows as the reference's _pieces
+    takes).  fp32 and CPU tensors take the reference's torch ops."""
+    if not _kernel_rows(x):
+        return scale_shift_(rms(x, weight, eps), shift, scale, segments)
+    from .. import _lib
+
+    m, hid = x.shape
+    x = _aligned_rows(x)
+    shift, scale = _aligned_rows(shift), _aligned_rows(scale)
+    if scale.dtype != shift.dtype:
+        scale = scale.to(shift.dtype)
+    if shift.stride(0) != scale.stride(0) or shift.shape != scale.shape or shift.shape[1] != hid:
+        shift, scale = shift.contiguous(), scale.contiguous()
+    w = weight.contiguous()
+    n_rows = shift.shape[0]
+    table, n_seg, token_rows = _segment_args(segments, m, n_rows, x.device)
+    h = torch.empty(m, hid, dtype=x.dtype, device=x.device)
+    L = _lib.lib()
+    _lib.check(L.h3b_rms_modulate(x.data_ptr(), _lib.act_code(x.dtype), x.stride(0), m, hid, w.data_ptr(),
+                                  _lib.act_code(w.dtype), float(eps), shift.data_ptr(), scale.data_ptr(), shift.stride(0),
+                                  n_rows, _lib.act_code(shift.dtype), table, n_seg, _lib.ptr(token_rows), h.data_ptr(), hid,
+                                  _lib.stream_ptr(x.device)), "rms_modulate")
+    return h
+
+
 def gate_(x: torch.Tensor, gate: torch.Tensor, other: torch.Tensor, segments: Sequence[Segment]) -> torch.Tensor:
+    """x[a:b] += other[a:b] * gate[row] per segment, in place (model.py:111-115): the fused kernel for bf16/fp16 CUDA
+    rows (bit-identical to torch's addcmul_), the reference's torch ops otherwise."""
+    if _kernel_rows(x) and other.shape == x.shape and other.dtype == x.dtype and x.stride(1) == 1 and x.stride(0) % 8 == 0 \
+            and x.data_ptr() % 16 == 0:
+        from .. import _lib
+
+        m, hid = x.shape
+        other, g = _aligned_rows(other), _aligned_rows(gate)
+        table, n_seg, token_rows = _segment_args(segments, m, g.shape[0], x.device)
+        _lib.check(_lib.lib().h3b_gate_residual(x.data_ptr(), _lib.act_code(x.dtype), x.stride(0), other.data_ptr(),
+                                                other.stride(0), m, hid, g.data_ptr(), g.stride(0), g.shape[0],
+                                                _lib.act_code(g.dtype), table, n_seg, _lib.ptr(token_rows),
+                                                _lib.stream_ptr(x.device)), "gate_residual")
+        return x
     for a, b, row in segments:
         if b > a:
             x[a:b].addcmul_(other[a:b], gate[row].to(x.dtype))
@@ -140,9 +209,9 @@ class DiTBlock:
     def __call__(self, x: torch.Tensor, w: BlockWeights, mod: Modulation, segments: Sequence[Segment], cos: torch.Tensor,
                  sin: torch.Tensor, spec: Optional[ShardSpec] = None) -> torch.Tensor:
         """x: [S_local, hidden] residual stream (updated in place and returned); cos/sin: [S_local, half] for these rows."""
-        h = scale_shift_(rms(x, w.norm1, self.norm_eps), mod.shift_a, mod.scale_a, segments)
+        h = rms_modulate(x, w.norm1, self.norm_eps, mod.shift_a, mod.scale_a, segments)
         gate_(x, mod.gate_a, self.attention(h, w, cos, sin, spec), segments)
-        h = scale_shift_(rms(x, w.norm2, self.norm_eps), mod.shift_m, mod.scale_m, segments)
+        h = rms_modulate(x, w.norm2, self.norm_eps, mod.shift_m, mod.scale_m, segments)
         return gate_(x, mod.gate_m, self.mlp(h, w), segments)
 
 
