@@ -37,6 +37,7 @@ SWEEP = [(5120, 5120), (5120, 13824), (13824, 5120)]  # (K, N)
 MS = [256, 2048, 16384, 65536]
 METRIC = "W4A8 qlinear int8 TOPS"
 WORKLOADS = ("sweep", "block", "stream", "longseq")
+GEMM_DRAM_BYTES_PER_OP = 349.907712e6 / (2.0 * 16384 * 5120 * 5120)
 HID, HEADS, HEAD_DIM, FFN = 5120, 40, 128, 13824  # DiT width, attention heads x head dim, SwiGLU width
 BLOCK_LINEARS = [(HID, 3 * HID), (HID, HID), (HID, 2 * FFN), (FFN, HID)]  # (K, N): qkv, out, fc1, fc2 (SwiGLU input)
 BLOCK_OPS_PER_TOKEN = sum(2.0 * k * n for k, n in BLOCK_LINEARS)  # 634.4 M
@@ -104,25 +105,57 @@ class ClockSampler:
         self.proc = None
 
     def start(self):
+        """Start sampling and wait (up to 5 s) for the first sample, so the timed region that follows is covered."""
+        import threading
+
+        self.lines, self.t_begin, self.t_end = [], None, None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "50", "-i", self.sel], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                                          text=True)
         except OSError:
             self.proc = None
+            return
+        first = threading.Event()
+
+        def reader():
+            for line in self.proc.stdout:
+                self.lines.append((time.monotonic(), line))
+                first.set()
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        first.wait(5.0)
+
+    def begin(self):
+        self.t_begin = time.monotonic()
+
+    def end(self):
+        self.t_end = time.monotonic()
 
     def stop(self):
+        """Median SM clock and active throttle reasons of the samples taken between begin() and end() (the nearest
+        sample when the region is shorter than the 50 ms sampling period)."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+        self.thread.join(timeout=5)
+        lines = list(self.lines)
+        b = self.t_begin if self.t_begin is not None else -1e18
+        e = self.t_end if self.t_end is not None else 1e18
+        inside = [ln for t, ln in lines if b <= t <= e + 0.05]
+        window = "timed region"
+        if not inside and lines:
+            mid = (b + e) / 2 if self.t_begin is not None and self.t_end is not None else lines[-1][0]
+            inside = [min(lines, key=lambda tl: abs(tl[0] - mid))[1]]
+            window = "nearest sample (timed region shorter than the sampling period)"
         sm, smax, power, reasons = [], [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in out.strip().splitlines():
+        for line in inside:
             f = [c.strip() for c in line.split(",")]
             if len(f) < 8:
                 continue
@@ -136,7 +169,8 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "power_w_max": max(power) if power else None, "samples": len(sm), "reasons": sorted(reasons)}
+                "power_w_max": max(power) if power else None, "samples": len(sm), "window": window,
+                "reasons": sorted(reasons)}
 
 
 # ------------------------------------------------------------------------------------------------ CPU (oracle) leg
@@ -393,12 +427,14 @@ def run_dit(args, rank, world, local):
     clocks = ClockSampler(local)
     clocks.start()
     barrier()
+    clocks.begin()
     lin.on = True
     t0.record(stream)
     for _ in range(args.steps):
         out = forward(x0)
     t1.record(stream)
     barrier()
+    clocks.end()
     lin.on = False
     clk = clocks.stop()
     t_local = torch.tensor([t0.elapsed_time(t1)], device=dev, dtype=torch.float64)
@@ -529,11 +565,14 @@ def run_stream(args, rank, world, local):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             if clocks:
                 clocks.start()
+                clocks.begin()
             e0.record(stream)
             for _ in range(args.steps):
                 y = forward(p, compute)
             e1.record(stream)
             torch.cuda.synchronize(dev)
+            if clocks:
+                clocks.end()
             clk = clocks.stop() if clocks else None
             s1 = p.stats()
             d = {k: s1[k] - s0[k] for k in ("acquires", "waits", "wait_s", "copies", "bytes")}
@@ -620,7 +659,7 @@ def run_stream(args, rank, world, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="h3b", choices=["h3b", "reference"])
     ap.add_argument("--ms", default=",".join(map(str, MS)))
@@ -719,11 +758,13 @@ def run_sweep(args, rank, world, local):
     clocks = ClockSampler(local)
     clocks.start()
     barrier()
+    clocks.begin()
     t0.record(stream)
     for s in range(args.steps):
         step(evs[s])
     t1.record(stream)
     barrier()
+    clocks.end()
     clk = clocks.stop()
     elapsed_ms = t0.elapsed_time(t1)
     t_local = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
@@ -751,15 +792,10 @@ def run_sweep(args, rank, world, local):
     gemm_tops = ops_step / (tot["gemm"] * 1e-3) / 1e12
     rotq_bytes = sum(3.0 * m * k + 4.0 * m for (k, _, m) in points)
     rotq_gbs = rotq_bytes / (tot["rotq"] * 1e-3) / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "traffic.json"
-    if tf.exists():
-        try:
-            t = json.loads(tf.read_text()).get("gemm_i8_kernel")
-            if t and t.get("bytes_per_op"):
-                traffic = t["bytes_per_op"] * ops_step / len(points)  # average bytes per GEMM launch at this workload
-        except Exception:
-            traffic = None
+    # DRAM bytes (read + write) per algorithmic op of the GEMM, from the ncu capture summarised in
+    # profiles/gemm_i8_kernel_sweep_m16384.md (K = N = 5120, M = 16384: 349.9 MB for 859.0 GOP), scaled to the average
+    # GEMM launch of this sweep
+    traffic = GEMM_DRAM_BYTES_PER_OP * ops_step / len(points)
 
     # ---- e2e through the public API with pinned host buffers (copies inside the timed region)
     e2e = None
