@@ -14,6 +14,7 @@
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the mainloop of tile i + 1.
 // Every mbarrier wait is bounded (h3b_common.cuh): a lost arrival makes the kernel raise the device flag and exit.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "h3b_common.cuh"
@@ -269,6 +270,172 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------------ CTA-pair variant
+// 256 x 256 output tiles on a cluster of two CTAs (one per SM of a TPC) with tcgen05.mma.cta_group::2: CTA r holds A rows
+// [128 r, 128 r + 128) and B rows (= output columns) [128 r, 128 r + 128) of the tile in its own shared memory, the
+// leader (rank 0) issues one 256 x 256 x 32 MMA that reads both CTAs' halves, and each CTA's TMEM receives its 128 rows
+// x 256 columns.  Per SM and per MMA the tensor core reads 4 KB of A and 4 KB of B from shared memory (the 1-CTA
+// 128 x 256 tile reads 4 + 8 KB), the co-limit the 1-CTA kernel hits.
+//   full[s]    leader only: one arrive.expect_tx (both CTAs' bytes) + the TMA bytes of both CTAs
+//   empty[s]   both CTAs: the leader's tcgen05.commit arrives on both
+//   tfull[b]   both CTAs: accumulator b is complete (leader's commit, both CTAs)
+//   tempty[b]  leader only: 2 x 128 epilogue threads (the peer's arrive remotely) have drained accumulator b
+constexpr int P_BN = 256;      // output columns per pair tile (N of the MMA)
+constexpr int P_BM = 2 * BM;   // output rows per pair tile
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = BM * BK;           // this CTA's A half per stage
+constexpr int P_B_BYTES = (P_BN / 2) * BK;   // this CTA's B half per stage
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_TMEM_COLS = 2 * P_BN;
+constexpr int P_SMEM = 1024 + P_STAGES * P_STAGE_BYTES + 256;
+constexpr uint32_t P_IDESC = idesc_i8(P_BM, P_BN);
+
+template <int OUT, bool BIAS, int QMODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const float* __restrict__ xs, const float* __restrict__ sch, const void* __restrict__ bias,
+                        void* __restrict__ out, int64_t ldo, int M, int N, int K, int gn) {
+  extern __shared__ __align__(1024) unsigned char gemm_smem[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + P_STAGES * P_A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + P_STAGES * P_B_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mdone = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int m_tiles = (M + P_BM - 1) / P_BM, n_tiles = (N + P_BN - 1) / P_BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * 128);
+    }
+    mbar_init(mdone, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, P_TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any remote arrive or MMA
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------------------------------------------------------- TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      long long fills = 0;
+      for (int tile = pair; tile < num_tiles; tile += npairs) {
+        int mt, nt;
+        tile_coords(tile, m_tiles, n_tiles, gn, mt, nt);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          const uint32_t bar = mapa_rank(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(sA + stage * P_A_BYTES, &tmA, bar, kb * BK, mt * P_BM + static_cast<int>(rank) * BM);
+          tma_load_2d_pair(sB + stage * P_B_BYTES, &tmB, bar, kb * BK, nt * P_BN + static_cast<int>(rank) * (P_BN / 2));
+          ++fills;
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+      // drain: this CTA's last loads must have landed before it may exit.  Their bytes count on the leader's full
+      // barriers, which only the leader can wait on; the peer waits for the leader's MMAs to release the stages instead.
+      for (long long j = fills > P_STAGES ? fills - P_STAGES : 0; j < fills; ++j) {
+        if (leader) {
+          if (!mbar_wait_drain(&full[j % P_STAGES], static_cast<uint32_t>((j / P_STAGES) & 1))) break;
+        } else {
+          if (!mbar_wait_drain(&empty[j % P_STAGES], static_cast<uint32_t>((j / P_STAGES) & 1))) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {  // ------------------------------------------------------- MMA issuer (leader only)
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
+        const int buf = it & 1;
+        if (!mbar_wait_cl(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * P_BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * P_A_BYTES), b0 = smem_u32(sB + stage * P_B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k)
+            mma_i8_pair(d_tmem, smem_desc_sw128(a0 + 32 * k), smem_desc_sw128(b0 + 32 * k), P_IDESC, (kb | k) != 0);
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit_pair(&tfull[buf], 0x3);
+      }
+      mma_commit_pair(mdone, 0x1);  // completes when every MMA issued above has finished
+      mbar_wait_drain(mdone, 0);
+    }
+  } else {  // -------------------------------------------------------------------------------------- epilogue (both CTAs)
+    const int quad = warp & 3;
+    const size_t osz = OUT == OUT_FP32 || OUT == OUT_S32 ? 4 : 2;
+    const bool vec_ok = (ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    const uint32_t tempty_leader0 = mapa_rank(smem_u32(&tempty[0]), 0), tempty_leader1 = mapa_rank(smem_u32(&tempty[1]), 0);
+    int it = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
+      const int buf = it & 1;
+      const bool ok = mbar_wait(&tfull[buf], (it >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      int mt, nt;
+      tile_coords(tile, m_tiles, n_tiles, gn, mt, nt);
+      const int row = mt * P_BM + static_cast<int>(rank) * BM + quad * 32 + lane;
+      const float xsr = (OUT != OUT_S32 && row < M) ? xs[row] : 0.f;
+      char* orow = static_cast<char*>(out) + static_cast<size_t>(row) * static_cast<size_t>(ldo) * osz;
+#pragma unroll 1
+      for (int c = 0; c < P_BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * P_BN + c * 32), r);
+        tmem_ld_wait();
+        const int n0 = nt * P_BN + c * 32;
+        if (row < M && n0 < N) epilogue_row32<OUT, BIAS, QMODE>(r, xsr, sch, bias, orow, n0, min(32, N - n0), vec_ok);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(buf ? tempty_leader1 : tempty_leader0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its pair may still read its shared memory or arrive on its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, P_TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -340,6 +507,63 @@ static int launch_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   return check_launch("gemm_i8_kernel");
 }
 
+template <int OUT, bool BIAS, int QMODE>
+static int launch_gemm_pair(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, const float* xs, const float* sch,
+                            const void* bias, void* out, int64_t ldo, int M, int N, int K, cudaStream_t st) {
+  CUtensorMap ta, tb;
+  int rc = make_map(&ta, a, K, M, lda, BM);
+  if (rc) return rc;
+  rc = make_map(&tb, b, K, N, ldb, P_BN / 2);
+  if (rc) return rc;
+  auto kern = gemm_i8_pair_kernel<OUT, BIAS, QMODE>;
+  static std::atomic<unsigned long long> attr_done{0};
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_done.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm pair)");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74, 1, 1);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = P_SMEM;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    max_pairs[dev & 63] = n;
+    attr_done.fetch_or(bit);
+  }
+  const int tiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+  const int pairs = tiles < max_pairs[dev & 63] ? tiles : max_pairs[dev & 63];
+  const int n_tiles = (N + P_BN - 1) / P_BN;
+  int gn = static_cast<int>((24ll << 20) / (static_cast<int64_t>(P_BN) * K));
+  gn = gn < 1 ? 1 : (gn > n_tiles ? n_tiles : gn);
+  kern<<<2 * pairs, 192, P_SMEM, st>>>(ta, tb, xs, sch, bias, out, ldo, M, N, K, gn);
+  return check_launch("gemm_i8_pair_kernel");
+}
+
+// The CTA-pair kernel for shapes that fill the GPU with 256 x 256 tiles; H3B_GEMM_PAIR=0 in the environment keeps the
+// 1-CTA kernel (read once per process; for comparisons).
+static bool pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("H3B_GEMM_PAIR");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 // Largest N tile that still gives every SM a tile; the smallest one otherwise.
 static int pick_bn(int M, int N) {
   const int sms = num_sms();
@@ -353,6 +577,8 @@ static int pick_bn(int M, int N) {
 template <int OUT, bool BIAS, int QMODE>
 static int dispatch_bn(int bn, const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, const float* xs,
                        const float* sch, const void* bias, void* out, int64_t ldo, int M, int N, int K, cudaStream_t st) {
+  if (bn == 256 && M >= P_BM && pair_enabled())
+    return launch_gemm_pair<OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
   switch (bn) {
     case 256: return launch_gemm<256, OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
     case 128: return launch_gemm<128, OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
