@@ -300,6 +300,65 @@ def run_reference_dit(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------ torch GPU path
+def torch_path_linear(x, w, n_rows_budget=128 << 20):
+    """The reference's own portable CUDA path restated on library kernels (qlinear.py:_TorchRunner :380-405): decode
+    the int8 grid with the generic-scale formula (:193-199), then per token chunk (the :391 int32 budget) the tiled
+    bf16 x H rotation with fp32 output (:84-104), the "ck" quantiser (:278-292), cuBLASLt torch._int_mm (:236-247) and
+    the (acc * xs) * s_ch epilogue (:400-401).  A measurement baseline for the B200 kernels, never the product path."""
+    import torch
+
+    from minimax_h3_turbo_b200.h3.qlinear import hadamard_regular
+
+    n, k = w.q.shape[0], w.q.shape[1] * 2
+    q = w.q.view(torch.uint8).to(torch.int32)
+    code = torch.empty(n, k, dtype=torch.int32, device=x.device)
+    code[:, 0::2] = q & 0xF
+    code[:, 1::2] = q >> 4
+    vals = w.codebook.float()[code].view(n, -1, w.group_size) * w.s_rel.float().unsqueeze(-1)
+    w8 = vals.view(n, k).round_().clamp_(-127, 127).to(torch.int8)
+    del q, code, vals
+    ws = w.s_ch.float().reshape(1, -1)
+    h = hadamard_regular(w.convrot, x.device, x.dtype)
+    m = x.shape[0]
+    out = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    step = max(32, n_rows_budget // (4 * n))
+    for a in range(0, m, step):
+        xc = x[a:a + step]
+        rows = xc.reshape(-1, w.convrot)
+        y32 = torch.empty(rows.shape[0], w.convrot, dtype=torch.float32, device=x.device)
+        for t in range(0, rows.shape[0], 4096):
+            torch.mm(rows[t:t + 4096], h, out=y32[t:t + 4096], out_dtype=torch.float32)
+        y32 = y32.view(xc.shape[0], k)
+        mn, mx = torch.aminmax(y32, dim=-1, keepdim=True)
+        xs = (torch.maximum(mx, -mn) / 127.0).clamp_(min=1e-30)
+        sc = xs.to(x.dtype)
+        sc = torch.where(sc == 0, torch.full_like(sc, torch.finfo(x.dtype).tiny), sc)
+        yq = y32.to(x.dtype).div_(sc).round_().clamp_(-128, 127).to(torch.int8)
+        acc = torch._int_mm(yq, w8.t())
+        torch.mul(torch.mul(acc, xs), ws, out=out[a:a + step])
+    return out
+
+
+def torch_path_rate(points, weights, acts, dev, reps=1):
+    """TOPS of the torch GPU path over the sweep (1 warm-up pass, then `reps` timed passes, CUDA events)."""
+    import torch
+
+    def one():
+        for (k, n, m) in points:
+            torch_path_linear(acts[(k, m)], weights[(k, n)][0])
+
+    one()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        one()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return ops_of(points) * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12
+
+
 # ------------------------------------------------------------------------------------------------ DiT workloads (GPU)
 def synthetic_block(seed, dev):
     """Random W4A8 block at DiT width (int4 group-128 from N(0, 0.02), fp16 scales) with bf16 norm weights."""
@@ -665,6 +724,7 @@ def main():
     ap.add_argument("--ms", default=",".join(map(str, MS)))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-torch-path", action="store_true", help="skip timing the torch restatement of the reference's CUDA path")
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--ref-rows", type=int, default=256)
     ap.add_argument("--detail", default="", help="write per-point timings to this JSON file")
@@ -833,6 +893,17 @@ def run_sweep(args, rank, world, local):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                "path": "qlinear.linear (public API) per point; pinned host input/output, copies on the compute stream"}
 
+    # ---- the reference's own CUDA algorithm on library kernels (cuBLAS rotation, cuBLASLt int8 GEMM), same GPU
+    torch_path = None
+    if world == 1 and not args.no_torch_path:
+        try:
+            torch_path = {"value": torch_path_rate(points, weights, acts, dev), "unit": "TOPS",
+                          "what": "the reference's portable CUDA path (decode, tiled cuBLAS rotation, ck quantiser, "
+                                  "torch._int_mm, epilogue) restated on torch ops, same sweep and GPU"}
+        except Exception as e:  # a library limitation must not cost the main measurement
+            torch_path = {"value": None, "error": repr(e)[:200]}
+            torch.cuda.synchronize(dev)
+
     # ---- CPU baseline (rank 0, single GPU only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -857,7 +928,7 @@ def run_sweep(args, rank, world, local):
                              "frac_of_sustained": gemm_tops / (2.0 * pk["bf16_sustained"]) if pk.get("bf16_sustained") else None},
                 "rotq_roofline": {"bound": "hbm", "kernel": "rotq_kernel", "achieved": rotq_gbs, "peak": pk["hbm_gbs"],
                                   "unit": "GB/s", "frac": rotq_gbs / pk["hbm_gbs"]},
-                "kernel_ms_per_step": tot, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "kernel_ms_per_step": tot, "cpu_baseline": cpu, "torch_gpu_path": torch_path, "e2e": e2e, "clocks": clk,
                 "gpu_launches": 3 * len(points) * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
