@@ -92,6 +92,19 @@ __device__ __forceinline__ float2 rne_bf16_fma(float2 v) {
   return __fadd2_rn(g, d);
 }
 constexpr float VELTKAMP_MAX = 1.2676506002282294e30f;  // 2^100
+
+// max(a, b, c), NaN operands ignored like fmaxf (one three-input instruction on sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// round half-to-even and saturate to [-128, 127]; the code in the low byte
+__device__ __forceinline__ uint32_t sat_s8(float v) {
+  int r;
+  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return static_cast<uint32_t>(r);
+}
 constexpr float RINT_MAGIC = 12582912.0f;  // 1.5 * 2^23: x + M rounds x to an integer (half-to-even) for |x| < 2^22
 
 // silu(gate) * up in dt, as torch computes it: x / (1 + exp(-x)) in fp32, rounded to dt; the product of the two dt
@@ -340,10 +353,15 @@ __global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __
           mA = fmaxf(mA, fabsf(y));
         }
       } else if constexpr (DT == DT_BF16 && MODE == MODE_CK) {
+        if constexpr (RG == 1) {  // split: both lanes are the same row
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          mA = fmaxf(mA, fabsf(v[i].x));
-          mB = fmaxf(mB, fabsf(v[i].y));
+          for (int i = 0; i < 16; ++i) mA = max3f(mA, fabsf(v[i].x), fabsf(v[i].y));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            mA = max3f(mA, fabsf(v[i].x), fabsf(v[i + 1].x));
+            mB = max3f(mB, fabsf(v[i].y), fabsf(v[i + 1].y));
+          }
         }
         if (fmaxf(mA, mB) < VELTKAMP_MAX) {
 #pragma unroll
@@ -433,14 +451,16 @@ __global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __
           const float2 q0 = __fmul2_rn(b, R2);
           float2 qd;
           if constexpr (DT == DT_BF16) {
-            // RNbf16(q0) is RNbf16(b / s); clamp at 127 first (same codes: every quotient > 127 ends at 127)
-            qd = rne_bf16_fma(make_float2(fminf(q0.x, 127.0f), fminf(q0.y, 127.0f)));
+            // RNbf16(q0) is RNbf16(b / s); the saturating conversion rounds half-to-even and clamps to [-128, 127]
+            // (on the XU pipe, which the rest of the kernel leaves idle)
+            qd = rne_bf16_fma(q0);
+            put(i, __byte_perm(sat_s8(qd.x), sat_s8(qd.y), 0x0040));
           } else {
             const float2 e = __ffma2_rn(q0, nS2, b);
             qd = unpack2<DT>(clamp_q2<DT>(pack2<DT>(__ffma2_rn(e, R2, q0))));  // dt(RN(b / s)), clamped
+            const float2 rr = __fadd2_rn(qd, MG);  // rint, half-to-even
+            put(i, __byte_perm(__float_as_uint(rr.x), __float_as_uint(rr.y), 0x0040));
           }
-          const float2 rr = __fadd2_rn(qd, MG);  // rint, half-to-even
-          put(i, __byte_perm(__float_as_uint(rr.x), __float_as_uint(rr.y), 0x0040));
         }
       }
       if constexpr (G > 1) {
