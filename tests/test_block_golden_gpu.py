@@ -1,0 +1,50 @@
+"""The DiT block on the B200 kernels against the reference's own block (tests/golden/block_golden.npz).
+
+Stage by stage on the golden inputs: the fused RMSNorm + modulation (the row sum's order differs from torch's
+F.rms_norm: rare one-ulp differences), the W4A8 qkv linear (the reference's codes: near-identical outputs), the fused
+q/k norm + RoPE (the reference's "torch" form; the rsqrt of CPU and GPU may differ in the last bit), then the whole block
+(attention through cuDNN instead of the CPU math kernel: bf16-level differences)."""
+import pytest
+import torch
+
+from minimax_h3_turbo_b200.h3 import block as blk
+from minimax_h3_turbo_b200.h3 import qlinear as ql
+from minimax_h3_turbo_b200.h3 import rope
+
+import block_golden_util as bg  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+def _ulp_stats(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    diff = (a - b).abs()
+    ulp = torch.maximum(a.abs(), b.abs()).clamp_min(1e-30) * 2.0 ** -7  # one bf16 ulp is at most 2^-7 relative
+    return (diff > 0).float().mean().item(), (diff / ulp).max().item()
+
+
+def test_stages_against_the_reference_block():
+    w, mod, segs, (hid, heads, hd, ffn), (eps, qk_eps), t = bg.load(DEV)
+    h1 = blk.rms_modulate(t["x"], w.norm1, eps, mod.shift_a, mod.scale_a, segs)
+    frac, worst = _ulp_stats(h1, t["h1"])
+    assert frac < 1e-3 and worst <= 2.0, (frac, worst)
+
+    qkv = ql.linear(t["h1"], w.qkv)
+    frac, _ = _ulp_stats(qkv, t["qkv"])
+    rel = ((qkv.float() - t["qkv"].float()).norm() / t["qkv"].float().norm()).item()
+    assert frac < 0.02 and rel < 1e-3, (frac, rel)
+
+    normed = t["qkv"].clone()
+    q, k, _ = (u.view(-1, heads, hd) for u in normed.split(heads * hd, dim=-1))
+    rope.norm_rope_(q, k, w.q_norm, w.k_norm, qk_eps, t["cos"], t["sin"], impl="b200")
+    frac, worst = _ulp_stats(normed, t["qkv_normed"])
+    assert frac < 1e-3 and worst <= 2.0, (frac, worst)
+
+
+def test_block_against_the_reference_block():
+    w, mod, segs, (hid, heads, hd, ffn), (eps, qk_eps), t = bg.load(DEV)
+    y = blk.DiTBlock(heads, hd, eps, qk_eps)(t["x"].clone(), w, mod, segs, t["cos"], t["sin"])
+    upd, ref = y.float() - t["x"].float(), t["y"].float() - t["x"].float()
+    rel = ((upd - ref).norm() / ref.norm()).item()
+    assert torch.isfinite(y.float()).all() and rel < 2e-2, rel
