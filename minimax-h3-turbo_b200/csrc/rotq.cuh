@@ -33,6 +33,11 @@
 
 #include "h3b_common.cuh"
 
+// Threads a CTA should at least have: row groups are added to a CTA until it reaches this (build-time tuning knob).
+#ifndef H3B_ROTQ_MIN_THREADS
+#define H3B_ROTQ_MIN_THREADS 128
+#endif
+
 namespace h3b {
 
 enum { DT_BF16 = 0, DT_FP16 = 1, DT_FP32 = 2 };
@@ -495,7 +500,7 @@ static int launch_t(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q,
   constexpr int MAXT = SPLIT ? 512 : 1024;
   using T = typename std::conditional<DT == DT_FP32, double, float2>::type;
   const int tpr = static_cast<int>(SPLIT ? K / 32 : K / 16);
-  int pairs = tpr >= 256 ? 1 : (256 + tpr - 1) / tpr;
+  int pairs = tpr >= H3B_ROTQ_MIN_THREADS ? 1 : (H3B_ROTQ_MIN_THREADS + tpr - 1) / tpr;
   while (pairs > 1 && pairs * tpr > MAXT) --pairs;
   const int threads = pairs * tpr;
   const size_t nblk = G > 1 ? static_cast<size_t>(threads) / G : 0;  // no exchange for blocks inside one thread
