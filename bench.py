@@ -467,7 +467,7 @@ def run_dit(args, rank, world, local):
     x0 = torch.randn(tokens, HID, generator=gx, device=dev).to(torch.bfloat16)[a:b].contiguous()
     x = torch.empty_like(x0)
     lin = TimedLinear()
-    block = blk.DiTBlock(HEADS, HEAD_DIM, linear=lin)
+    block = blk.DiTBlock(HEADS, HEAD_DIM, linear=lin, kv_exchange=args.kv_exchange)
     stream = torch.cuda.current_stream(dev)
 
     def forward(xin):
@@ -543,7 +543,9 @@ def run_dit(args, rank, world, local):
     attn_flops = nb * 4.0 * rows * tokens * HEADS * HEAD_DIM
     fields = dit_common_fields(peaks(), lin_ops, lin.ms(), attn_flops, t_ms if world == 1 else t0.elapsed_time(t1), args.steps)
     if rank == 0:
-        cfg = dict(cfg, parallelism=f"token-shard x{world} (contiguous rows, K/V all-gather per block, output all-gather)",
+        exch = "K/V shards passed round a ring of the ranks, overlapped with attention" if args.kv_exchange == "ring" \
+            else "K/V all-gather per block"
+        cfg = dict(cfg, parallelism=f"token-shard x{world} (contiguous rows, {exch}, output all-gather)",
                    rows_per_rank=[e - s for s, e in (blk.shard_rows(tokens, world, r) for r in range(world))],
                    l2="inputs larger than L2 (each block streams ~0.6 GB of weights+activations per rank)")
         line = {"metric": metric, "value": tokens * args.steps / (t_ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
@@ -734,6 +736,8 @@ def main():
     ap.add_argument("--workload", default="sweep", choices=WORKLOADS,
                     help="sweep: config 2 (default); block: config 3; stream: config 4; longseq: config 5")
     ap.add_argument("--store-dir", default="", help="stream workload: directory for the temporary ~7.9 GB h3t store")
+    ap.add_argument("--kv-exchange", default="ring", choices=["ring", "gather"],
+                    help="block/longseq on several GPUs: key/value shards passed round a ring (overlapped) or all-gathered")
     args = ap.parse_args()
     args.ms = [int(v) for v in args.ms.split(",") if v]
     rank, world, local = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))

@@ -102,6 +102,17 @@ int h3b_gate_residual(void* x, int x_dtype, int64_t ldx, const void* other, int6
                       const void* gate, int64_t ldm, int64_t n_rows, int m_dtype, const int32_t* segments, int n_segments,
                       const int32_t* token_rows, void* stream);
 
+/* Merge softmax attention computed over disjoint key sets (no reference counterpart: the ring key/value exchange of
+ * the token-sharded DiT block, whose single-GPU form is one attention call, model.py:196-228).  For every head h and
+ * query q: L' = log(exp(L) + exp(l)), A = A exp(L - L') + fp32(o) exp(l - L'), L = L'.
+ *   acc    fp32 [heads, queries, head_dim] running output;  acc_lse fp32 [heads, queries] running log-sum-exp
+ *   o      bf16 attention output over the next key set, element (h, q, d) at o + h*o_head_stride + q*o_query_stride + d
+ *   lse    fp32 [heads, queries] its log-sum-exp (natural log);  first != 0: (acc, acc_lse) = (o, lse)
+ *   out    optional bf16 [queries, heads * head_dim] (row stride ldo): the merged result, written instead of acc */
+int h3b_attn_merge(float* acc, float* acc_lse, const void* o, int64_t o_head_stride, int64_t o_query_stride,
+                   const float* lse, int64_t heads, int64_t queries, int head_dim, int first, void* out, int64_t ldo,
+                   void* stream);
+
 /* int4 codebook indices + group scales -> the exact int8 grid [N, K] (row stride ldg bytes).
  * Replaces decode_int8_grid / _decode_rows / _pair_lut (qlinear.py:157-204).
  *   q4     [N, ldq4 bytes] packed nibbles, low nibble first (types.py:14-16)

@@ -43,6 +43,8 @@ _SIGNATURES = {
                           _i64, _int, _c_void_p, _int, _c_void_p, _c_void_p, _i64, _c_void_p], _int),
     "h3b_gate_residual": ([_c_void_p, _int, _i64, _c_void_p, _i64, _i64, _int, _c_void_p, _i64, _i64, _int, _c_void_p, _int,
                            _c_void_p, _c_void_p], _int),
+    "h3b_attn_merge": ([_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _int, _int, _c_void_p, _i64,
+                        _c_void_p], _int),
     "h3b_decode_grid": ([_c_void_p, _i64, _i64, _i64, _c_void_p, _int, _i64, _c_void_p, _int, _c_void_p, _i64, _c_void_p], _int),
     "h3b_int8_gemm_s32": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p], _int),
     "h3b_gemm_workspace_bytes": ([_i64, _i64, _i64], _sz),

@@ -27,6 +27,7 @@ int check_launch(const char* what) {
 
 }  // namespace h3b
 
+#include "attn_merge.cuh"
 #include "decode.cuh"
 #include "gemm_sm100.cuh"
 #include "rmsmod.cuh"
@@ -200,6 +201,17 @@ int h3b_gate_residual(void* x, int x_dtype, int64_t ldx, const void* other, int6
       return fail(H3B_ERR_ARG, "gate_residual: a segment has a negative bound, ends before it starts, or names a row >= n_rows");
   return gate_residual_launch(x, x_dtype, ldx, other, ldo, M, hidden, gate, ldm, m_dtype, segments, n_segments, token_rows,
                               static_cast<cudaStream_t>(stream));
+}
+
+int h3b_attn_merge(float* acc, float* acc_lse, const void* o, int64_t o_head_stride, int64_t o_query_stride,
+                   const float* lse, int64_t heads, int64_t queries, int head_dim, int first, void* out, int64_t ldo,
+                   void* stream) {
+  if (heads < 0 || queries < 0) return fail(H3B_ERR_ARG, "attn_merge: negative size");
+  if (heads == 0 || queries == 0) return H3B_OK;
+  if (!acc || !acc_lse || !o || !lse) return fail(H3B_ERR_ARG, "attn_merge: null pointer");
+  if (out && ldo < heads * head_dim) return fail(H3B_ERR_ARG, "attn_merge: output row stride below heads * head_dim");
+  return attn_merge_launch(acc, acc_lse, o, o_head_stride, o_query_stride, lse, heads, queries, head_dim, first, out, ldo,
+                           static_cast<cudaStream_t>(stream));
 }
 
 int h3b_decode_grid(const void* q4, int64_t N, int64_t K, int64_t ldq4, const void* s_rel, int s_dtype, int64_t lds,

@@ -171,11 +171,87 @@ def gather_rows(x: torch.Tensor, spec: ShardSpec) -> torch.Tensor:
     return torch.cat([out[r * cap: r * cap + sizes[r]] for r in range(spec.world)])
 
 
+def attention_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Softmax attention of q [1, H, Sq, D] over k, v [1, H, Sk, D] -> (o [1, H, Sq, D] in q.dtype, lse [1, H, Sq] fp32,
+    the natural-log sum of exp of the scaled scores): torch's cuDNN fused kernel on CUDA, the explicit fp32 softmax
+    elsewhere (the CPU ranks of the sharding tests)."""
+    if q.is_cuda:
+        r = torch.ops.aten._scaled_dot_product_cudnn_attention(q, k, v, None, True)
+        return r[0], r[1].reshape(q.shape[:-1]).to(torch.float32)
+    sc = torch.matmul(q.float(), k.float().transpose(-1, -2)) * (q.shape[-1] ** -0.5)
+    lse = torch.logsumexp(sc, dim=-1)
+    return torch.matmul(torch.exp(sc - lse.unsqueeze(-1)), v.float()).to(q.dtype), lse
+
+
+def merge_attention(acc: Optional[torch.Tensor], acc_lse: Optional[torch.Tensor], o: torch.Tensor,
+                    lse: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Combine attention over disjoint key sets: softmax weights renormalised by the log-sum-exps, in fp32."""
+    if acc is None:
+        return o.float(), lse
+    new = torch.logaddexp(acc_lse, lse)
+    acc = acc.mul_(torch.exp(acc_lse - new).unsqueeze(-1)).add_(o.float() * torch.exp(lse - new).unsqueeze(-1))
+    return acc, new
+
+
+def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: ShardSpec) -> torch.Tensor:
+    """Attention of this rank's queries over every rank's keys and values, with the key/value shards passed round a
+    ring of the ranks (P - 1 point-to-point steps) while the attention over the shard already here runs: the transfer
+    of step s + 1 overlaps the attention of step s.  q, k, v: [S_local, H, D]; returns [S_local, H, D] in q.dtype."""
+    import torch.distributed as dist
+
+    p_, r_ = spec.world, spec.rank
+    sizes = [b - a for a, b in (shard_rows(spec.total, p_, i) for i in range(p_))]
+    cap = max(sizes)
+    s, h, d = k.shape
+    bufs = [torch.zeros(2, cap, h, d, dtype=k.dtype, device=k.device) for _ in range(2)]
+    bufs[0][0, :s] = k
+    bufs[0][1, :s] = v
+    qh = q.transpose(0, 1).unsqueeze(0).contiguous()
+    fused = q.is_cuda and q.dtype == torch.bfloat16 and d in (64, 128, 256)
+    if fused:  # running output / log-sum-exp for the merge kernel, and the final [S, H * D] rows
+        from .. import _lib
+
+        acc = torch.empty(h, s, d, dtype=torch.float32, device=q.device)
+        acc_lse = torch.empty(h, s, dtype=torch.float32, device=q.device)
+        final = torch.empty(s, h * d, dtype=q.dtype, device=q.device)
+    else:
+        acc = acc_lse = None
+    nxt, prv = (r_ + 1) % p_, (r_ - 1) % p_
+    for step in range(p_):
+        cur = bufs[step % 2]
+        reqs = []
+        if step < p_ - 1:
+            reqs = dist.batch_isend_irecv([dist.P2POp(dist.isend, cur, nxt, group=spec.group),
+                                           dist.P2POp(dist.irecv, bufs[(step + 1) % 2], prv, group=spec.group)])
+        n = sizes[(r_ - step) % p_]  # the shard in `cur` came from rank r - step
+        o, lse = attention_lse(qh, cur[0, :n].transpose(0, 1).unsqueeze(0), cur[1, :n].transpose(0, 1).unsqueeze(0))
+        if fused:
+            lse = lse.reshape(h, s).contiguous()
+            if o.stride(3) != 1:
+                o = o.contiguous()
+            last = step == p_ - 1
+            _lib.check(_lib.lib().h3b_attn_merge(acc.data_ptr(), acc_lse.data_ptr(), o.data_ptr(), o.stride(1), o.stride(2),
+                                                 lse.data_ptr(), h, s, d, int(step == 0),
+                                                 final.data_ptr() if last else None, h * d,
+                                                 _lib.stream_ptr(q.device)), "attn_merge")
+        else:
+            acc, acc_lse = merge_attention(acc, acc_lse, o, lse)
+        for rq in reqs:
+            rq.wait()
+    if fused:
+        return final.view(s, h, d)
+    return acc[0].transpose(0, 1).to(q.dtype)
+
+
 class DiTBlock:
-    """Runs H3 DiT blocks on the W4A8 kernels.  heads / head_dim / eps as in H3Config."""
+    """Runs H3 DiT blocks on the W4A8 kernels.  heads / head_dim / eps as in H3Config.  kv_exchange: "ring" (key/value
+    shards passed round the ranks, overlapped with attention) or "gather" (one all-gather of K and V per block)."""
 
     def __init__(self, heads: int, head_dim: int, norm_eps: float = 1e-5, qk_norm_eps: float = 1e-5,
-                 precision: str = "a8", attn_chunk: Optional[int] = None, linear=None):
+                 precision: str = "a8", attn_chunk: Optional[int] = None, linear=None, kv_exchange: str = "ring"):
+        if kv_exchange not in ("ring", "gather"):
+            raise ValueError(f"kv_exchange must be 'ring' or 'gather', got {kv_exchange!r}")
+        self.kv_exchange = kv_exchange
         self.heads, self.head_dim = heads, head_dim
         self.norm_eps, self.qk_norm_eps, self.precision = norm_eps, qk_norm_eps, precision
         self.attn_chunk = attn_chunk
@@ -189,6 +265,8 @@ class DiTBlock:
         qkv = self._linear(h, w.qkv)
         q, k, v = (t.view(s, heads, hd) for t in qkv.split(inner, dim=-1))
         norm_rope_(q, k, w.q_norm, w.k_norm, self.qk_norm_eps, cos, sin)
+        if spec is not None and spec.world > 1 and self.kv_exchange == "ring":
+            return self._linear(ring_attention(q, k, v, spec).reshape(s, inner), w.out)
         if spec is not None and spec.world > 1:  # every query needs every key and value
             k = gather_rows(k.reshape(s, inner).contiguous(), spec).view(-1, heads, hd)
             v = gather_rows(v.reshape(s, inner).contiguous(), spec).view(-1, heads, hd)

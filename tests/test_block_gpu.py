@@ -114,3 +114,58 @@ def test_blocks_on_streamed_weights_equal_resident(tmp_path):
                     p.release(i)
                 p.end_forward()
                 assert torch.equal(x, y)
+
+
+def test_attention_over_key_chunks_merges_to_full_attention():
+    """cuDNN attention with its log-sum-exp over disjoint key chunks, merged, equals one attention call (the ring
+    exchange of the token-sharded block relies on it)."""
+    g = torch.Generator(device=DEV).manual_seed(3)
+    q, k, v = (torch.randn(1, 4, n, 128, generator=g, device=DEV).to(torch.bfloat16) for n in (300, 700, 700))
+    want = torch.nn.functional.scaled_dot_product_attention(q, k, v).float()
+    acc = lse = None
+    for a, b in ((0, 250), (250, 251), (251, 700)):
+        o, l_ = blk.attention_lse(q, k[:, :, a:b], v[:, :, a:b])
+        acc, lse = blk.merge_attention(acc, lse, o, l_)
+    assert _rel(acc, want) < 1e-2, _rel(acc, want)
+
+
+def test_ring_block_on_two_gpus_equals_one_gpu():
+    """Token-sharded DiT block over 2 GPUs (ring and gather exchanges) against the same block on one GPU; run by
+    torchrun in a child process when at least 2 GPUs are visible."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    here = Path(__file__).resolve().parent
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
+           "--master-port=29531", str(here / "helpers" / "ring_block_check.py")]
+    env = dict(__import__("os").environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "RING_OK" in r.stdout and "GATHER_OK" in r.stdout, r.stdout[-3000:]
+
+
+def test_fused_merge_kernel_equals_the_torch_merge():
+    from minimax_h3_turbo_b200 import _lib
+
+    g = torch.Generator(device=DEV).manual_seed(4)
+    h, sq, d = 3, 257, 128
+    q = torch.randn(1, h, sq, d, generator=g, device=DEV).to(torch.bfloat16)
+    kv = [(torch.randn(1, h, n, d, generator=g, device=DEV).to(torch.bfloat16),
+           torch.randn(1, h, n, d, generator=g, device=DEV).to(torch.bfloat16)) for n in (100, 37, 300)]
+    acc = torch.empty(h, sq, d, device=DEV)
+    lse_acc = torch.empty(h, sq, device=DEV)
+    out = torch.empty(sq, h * d, dtype=torch.bfloat16, device=DEV)
+    ref = ref_lse = None
+    for i, (k, v) in enumerate(kv):
+        o, lse = blk.attention_lse(q, k, v)
+        ref, ref_lse = blk.merge_attention(ref, ref_lse, o, lse)
+        lse = lse.reshape(h, sq).contiguous()
+        _lib.check(_lib.lib().h3b_attn_merge(acc.data_ptr(), lse_acc.data_ptr(), o.data_ptr(), o.stride(1), o.stride(2),
+                                             lse.data_ptr(), h, sq, d, int(i == 0),
+                                             out.data_ptr() if i == len(kv) - 1 else None, h * d,
+                                             _lib.stream_ptr(DEV)), "merge")
+    want = ref[0].transpose(0, 1).reshape(sq, h * d)
+    assert _rel(out, want) < 5e-3, _rel(out, want)
