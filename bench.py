@@ -553,7 +553,9 @@ def run_dit(args, rank, world, local):
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": cfg, **fields,
                 "linear_tops_whole_job": world * lin_ops * args.steps / (t_ms * 1e-3) / 1e12,
                 "output_finite": finite, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-                "gpu_launches": 3 * lin.calls}
+                # per block: 4 W4A8 linears (rotate+quantise, decode, GEMM each), 2 RMSNorm+modulation, 1 q/k norm+RoPE,
+                # 2 gated residuals, and with the ring exchange one attention merge per key shard
+                "gpu_launches": 3 * lin.calls + (5 + (world if world > 1 and args.kv_exchange == "ring" else 0)) * nb * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -789,6 +791,12 @@ def run_sweep(args, rank, world, local):
     codes = torch.empty(mmax * kmax, dtype=torch.int8, device=dev)
     xs = torch.empty(mmax, dtype=torch.float32, device=dev)
 
+    # small M: the W4A8 GEMM decodes the int4 weight in its producer warps (no decode pass); large M: decode pass, then
+    # the int8 GEMM -- exactly what h3b_w4a8_gemm (and qlinear.linear) do for each point
+    fused = {(k, n, m): bool(L.h3b_w4a8_gemm_decodes_in_kernel(m, n, k, weights[(k, n)][1].q.data_ptr(),
+                                                                weights[(k, n)][1].ldq, weights[(k, n)][1].s_dtype, 128))
+             for (k, n, m) in points}
+
     def step(evs=None):
         """One pass of the hot path over every sweep point: KA (rotate+quantise), decode, KB (GEMM + epilogue)."""
         for i, (k, n, m) in enumerate(points):
@@ -800,13 +808,20 @@ def run_sweep(args, rank, world, local):
             if evs is not None:
                 evs[i][1].record(stream)
             g = grids[(k, n)]
-            _lib.check(L.h3b_decode_grid(a.q.data_ptr(), n, k, a.ldq, a.s.data_ptr(), a.s_dtype, a.lds, a.cb.data_ptr(), 128,
-                                         g.data_ptr(), k, sp), "decode")
-            if evs is not None:
-                evs[i][2].record(stream)
             o = outs[(k, n, m)]
-            _lib.check(L.h3b_int8_gemm_epilogue(codes.data_ptr(), k, xs.data_ptr(), m, g.data_ptr(), k, a.s_ch.data_ptr(), None,
-                                                o.data_ptr(), _lib.BF16, n, n, k, 0, sp), "gemm")
+            if fused[(k, n, m)]:
+                if evs is not None:
+                    evs[i][2].record(stream)
+                _lib.check(L.h3b_w4a8_gemm(codes.data_ptr(), k, xs.data_ptr(), m, a.q.data_ptr(), a.ldq, a.s.data_ptr(),
+                                           a.s_dtype, a.lds, a.s_ch.data_ptr(), a.cb.data_ptr(), 128, None, o.data_ptr(),
+                                           _lib.BF16, n, n, k, 0, g.data_ptr(), g.numel(), sp), "w4a8 gemm")
+            else:
+                _lib.check(L.h3b_decode_grid(a.q.data_ptr(), n, k, a.ldq, a.s.data_ptr(), a.s_dtype, a.lds, a.cb.data_ptr(),
+                                             128, g.data_ptr(), k, sp), "decode")
+                if evs is not None:
+                    evs[i][2].record(stream)
+                _lib.check(L.h3b_int8_gemm_epilogue(codes.data_ptr(), k, xs.data_ptr(), m, g.data_ptr(), k, a.s_ch.data_ptr(),
+                                                    None, o.data_ptr(), _lib.BF16, n, n, k, 0, sp), "gemm")
             if evs is not None:
                 evs[i][3].record(stream)
 
@@ -849,7 +864,7 @@ def run_sweep(args, rank, world, local):
         tot["rotq"] += r
         tot["decode"] += d
         tot["gemm"] += g
-        per_point.append({"K": k, "N": n, "M": m, "rotq_ms": r, "decode_ms": d, "gemm_ms": g,
+        per_point.append({"K": k, "N": n, "M": m, "decode_in_gemm": fused[(k, n, m)], "rotq_ms": r, "decode_ms": d, "gemm_ms": g,
                           "gemm_tops": 2.0 * m * n * k / (g * 1e-3) / 1e12, "linear_tops": 2.0 * m * n * k / ((r + d + g) * 1e-3) / 1e12,
                           "rotq_gbs": (3.0 * m * k + 4 * m) / (r * 1e-3) / 1e9})
     ops_step = ops_of(points)
@@ -954,14 +969,15 @@ def run_sweep(args, rank, world, local):
         line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": t_max_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "int8", "data": "synthetic", "config": config_dict(args.ms, world),
-                "roofline": {"bound": "tensor", "kernel": "gemm_i8_kernel", "achieved": gemm_tops, "peak": int8_peak,
+                "roofline": {"bound": "tensor", "kernel": "int8 GEMM (gemm_i8_pair_kernel for large M, gemm_w4_kernel with "
+                                                           "the int4 decode for small M)", "achieved": gemm_tops, "peak": int8_peak,
                              "unit": "TOPS", "frac": gemm_tops / int8_peak, "traffic": traffic,
                              "peak_note": f"int8 dense = 2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s burst)",
                              "frac_of_sustained": gemm_tops / (2.0 * pk["bf16_sustained"]) if pk.get("bf16_sustained") else None},
                 "rotq_roofline": {"bound": "hbm", "kernel": "rotq_kernel", "achieved": rotq_gbs, "peak": pk["hbm_gbs"],
                                   "unit": "GB/s", "frac": rotq_gbs / pk["hbm_gbs"]},
                 "kernel_ms_per_step": tot, "cpu_baseline": cpu, "torch_gpu_path": torch_path, "e2e": e2e, "clocks": clk,
-                "gpu_launches": 3 * len(points) * args.steps}
+                "gpu_launches": sum(2 if fused[p] else 3 for p in points) * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

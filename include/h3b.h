@@ -145,6 +145,12 @@ int h3b_w4a8_gemm(const int8_t* qa, int64_t lda, const float* xs, int64_t M, con
 /* GEMM + epilogue on an already-decoded int8 weight grid [N, ldg bytes] (same epilogue contract as h3b_w4a8_gemm).
  * For callers that keep decoded grids resident (weights that never stream); no workspace.  Same reference lines as
  * h3b_w4a8_gemm (qlinear.py:396-405) with the decode (qlinear.py:194-204) hoisted out. */
+/* 1 when h3b_w4a8_gemm (and so h3b_w4a8_linear) decodes the int4 weight inside the GEMM's producer warps for this
+ * problem (few M tiles; fp8 e4m3 scales with group 16 or fp16/bf16/fp32 scales with group 128; 16-byte aligned packed
+ * rows), 0 when it runs a separate decode pass into the workspace first.  No reference counterpart (introspection). */
+int h3b_w4a8_gemm_decodes_in_kernel(int64_t M, int64_t N, int64_t K, const void* q4, int64_t ldq4, int s_dtype,
+                                    int group);
+
 int h3b_int8_gemm_epilogue(const int8_t* qa, int64_t lda, const float* xs, int64_t M, const int8_t* grid, int64_t ldg,
                            const float* s_ch, const void* bias, void* out, int out_dtype, int64_t ldo, int64_t N,
                            int64_t K, int quant_mode, void* stream);

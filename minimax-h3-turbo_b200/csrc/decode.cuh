@@ -5,6 +5,8 @@
 //   level[n, k]   = clamp(rint(fp32(codebook[nibble]) * fp32(s_rel[n, k / group])), -127, 127)   (half-to-even)
 //   fp8 scale bytes that are NaN decode to level 0 (the pair table's nan_to_num, :162).
 // One thread decodes 16 consecutive weights (8 packed bytes) of one row and stores them as one 16-byte vector.
+#pragma once
+
 #include "h3b_common.cuh"
 
 namespace h3b {

@@ -13,6 +13,8 @@
 //   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, scales, rounding, bias, 16-byte stores
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the mainloop of tile i + 1.
 // Every mbarrier wait is bounded (h3b_common.cuh): a lost arrival makes the kernel raise the device flag and exit.
+#pragma once
+
 #include <atomic>
 #include <cstdlib>
 #include <mutex>

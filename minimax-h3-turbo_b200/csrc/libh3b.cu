@@ -30,6 +30,7 @@ int check_launch(const char* what) {
 #include "attn_merge.cuh"
 #include "decode.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm_w4.cuh"
 #include "rmsmod.cuh"
 #include "rope.cuh"
 #include "rotq.cuh"
@@ -262,10 +263,18 @@ int h3b_w4a8_gemm(const int8_t* qa, int64_t lda, const float* xs, int64_t M, con
   if (!workspace || ws_bytes < need || !aligned(workspace, 256))
     return fail(H3B_ERR_ARG, "workspace must be 256-byte aligned and hold h3b_gemm_workspace_bytes() = " + std::to_string(need) + " bytes");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (w4_fused_ok(M, N, K, q4, ldq4, s_dtype, group))  // few M tiles: decode inside the GEMM's producer warps
+    return gemm_w4_launch(qa, lda, q4, ldq4, s_rel, s_dtype, lds, codebook, xs, s_ch, bias, out, out_dtype, ldo, M, N, K,
+                          quant_mode, st);
   int8_t* grid = static_cast<int8_t*>(workspace);
   rc = decode_launch(q4, N, K, ldq4, s_rel, s_dtype, lds, codebook, group, grid, K, st);
   if (rc) return rc;
   return gemm_launch(qa, lda, grid, K, xs, s_ch, bias, out, out_dtype, ldo, M, N, K, quant_mode, st);
+}
+
+int h3b_w4a8_gemm_decodes_in_kernel(int64_t M, int64_t N, int64_t K, const void* q4, int64_t ldq4, int s_dtype,
+                                    int group) {
+  return w4_fused_ok(M, N, K, q4, ldq4, s_dtype, group) ? 1 : 0;
 }
 
 int h3b_int8_gemm_epilogue(const int8_t* qa, int64_t lda, const float* xs, int64_t M, const int8_t* grid, int64_t ldg,

@@ -1,0 +1,65 @@
+"""The GEMM that decodes the int4 weight in its producer warps (small M) against the separate decode pass followed by
+the int8 GEMM, bit for bit: both scale formats it takes (fp16 group 128, fp8 e4m3 group 16), every output dtype, bias,
+both quantiser modes, ragged M, N and K."""
+import pytest
+import torch
+
+from minimax_h3_turbo_b200 import _lib
+from minimax_h3_turbo_b200.h3 import qlinear as ql
+from minimax_h3_turbo_b200.h3.synth import synthetic_w4a8
+from minimax_h3_turbo_b200.h3.types import W4A8Weight
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+def _fp8_weight(n, k, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    q = torch.randint(-128, 128, (n, k // 2), generator=g, device=DEV, dtype=torch.int8)
+    s_rel = (torch.rand(n, k // 16, generator=g, device=DEV) * 180 + 20).to(torch.float8_e4m3fn)
+    s_ch = torch.rand(n, generator=g, device=DEV) * 1e-3 + 1e-4
+    cb = torch.linspace(-1.0, 1.0, 16, device=DEV)
+    return W4A8Weight(q, s_rel, s_ch, cb, 16, 16 if k % 256 else 256)
+
+
+def _unfused(qa, xs, w, bias, out_dtype, mode):
+    a = ql._WeightArgs(w)
+    n, k = a.n, a.k
+    grid = torch.empty(n, k, dtype=torch.int8, device=DEV)
+    L = _lib.lib()
+    _lib.check(L.h3b_decode_grid(a.q.data_ptr(), n, k, a.ldq, a.s.data_ptr(), a.s_dtype, a.lds, a.cb.data_ptr(), a.group,
+                                 grid.data_ptr(), k, _lib.stream_ptr(DEV)), "decode")
+    out = torch.empty(qa.shape[0], n, dtype=out_dtype, device=DEV)
+    code = _lib.INT32 if out_dtype == torch.int32 else _lib.act_code(out_dtype)
+    b = None if bias is None or out_dtype == torch.int32 else bias.to(out_dtype).contiguous()
+    _lib.check(L.h3b_int8_gemm_epilogue(qa.data_ptr(), k, xs.data_ptr(), qa.shape[0], grid.data_ptr(), k,
+                                        a.s_ch.data_ptr(), _lib.ptr(b), out.data_ptr(), code, n, n, k, _lib.QMODE[mode],
+                                        _lib.stream_ptr(DEV)), "gemm")
+    return out
+
+
+@pytest.mark.parametrize("m,n,k,fmt,dt,bias,mode", [
+    (256, 5120, 5120, "fp16", torch.bfloat16, False, "ck"),
+    (256, 13824, 5120, "fp16", torch.bfloat16, True, "ck"),
+    (200, 5000, 13824, "fp16", torch.float32, False, "eager"),
+    (1024, 1536, 1536, "fp16", torch.bfloat16, True, "ck"),     # config 1
+    (77, 3072, 1056, "fp8", torch.bfloat16, False, "ck"),       # K not a multiple of 128
+    (300, 4096, 4096, "fp8", torch.float16, True, "eager"),
+    (64, 1000, 2048, "fp8", torch.int32, False, "ck"),
+])
+def test_decode_in_producer_equals_separate_decode(m, n, k, fmt, dt, bias, mode):
+    w = synthetic_w4a8(n, k, seed=n + k, device=DEV) if fmt == "fp16" else _fp8_weight(n, k, n + k)
+    a = ql._WeightArgs(w)
+    assert _lib.lib().h3b_w4a8_gemm_decodes_in_kernel(m, n, k, a.q.data_ptr(), a.ldq, a.s_dtype, a.group) == 1
+    g = torch.Generator(device=DEV).manual_seed(m)
+    qa = torch.randint(-128, 128, (m, k), generator=g, device=DEV, dtype=torch.int8)
+    xs = torch.rand(m, generator=g, device=DEV) * 0.05 + 1e-3
+    b = torch.randn(n, generator=g, device=DEV) if bias else None
+    fused = ql._gemm_codes(qa, xs, w, b, out_dtype=dt, quant_mode=mode)
+    assert torch.equal(fused, _unfused(qa, xs, w, b, dt, mode))
+
+
+def test_large_m_keeps_the_separate_decode():
+    w = synthetic_w4a8(5120, 5120, seed=1, device=DEV)
+    a = ql._WeightArgs(w)
+    assert _lib.lib().h3b_w4a8_gemm_decodes_in_kernel(16384, 5120, 5120, a.q.data_ptr(), a.ldq, a.s_dtype, a.group) == 0
