@@ -1,13 +1,13 @@
 // Kernel KB with the int4 weight decode in its producer warps (the small-M, weight-bandwidth-bound regime).
 //
 // Same product and epilogue as gemm_i8_kernel, but B arrives as the packed int4 codebook indices of the weight: TMA
-// brings a BN x 64-byte tile of packed nibbles per stage, four decoder warps turn it into the BN x 128 int8 levels the
+// brings a BN x 64-byte tile of packed nibbles per stage, eight decoder warps turn it into the BN x 128 int8 levels the
 // tensor core reads (level tables per scale group and byte permutes, exactly decode.cuh's levels), write them into the
 // stage's 128-byte-swizzled B tile, and arrive on the stage's barrier after a generic->async proxy fence.  The weight
 // crosses HBM once at 0.5 byte per element and no int8 grid is written.  Used when the M tiles are few (each B tile is
 // decoded once per M tile); for large M a separate decode pass followed by the CTA-pair kernel does less work.
 //
-// Warps: 0 TMA producer (A tile + packed B tile), 1 MMA issuer, 2-5 epilogue, 6-9 decoders (320 threads).
+// Warps: 0 TMA producer (A tile + packed B tile), 1 MMA issuer, 2-5 epilogue, 6-13 decoders (448 threads).
 //   pkfull[s]  packed tile of stage s landed (TMA bytes)
 //   full[s]    A bytes (TMA) + one arrival per decoder warp: the stage is ready for the MMA
 //   empty[s]   the MMAs of stage s finished (tcgen05.commit): A, B and the packed tile may be refilled
@@ -27,11 +27,12 @@ struct W4Cfg {
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 4096 + 512;  // ring + fp8 level tables + barriers
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
-  static constexpr int CPT = BN / 16;  // 16-weight chunks per decoder thread and stage (BN * 8 chunks / 128 threads)
+  static constexpr int DWARPS = 8;                 // decoder warps
+  static constexpr int CPT = BN * 8 / (32 * DWARPS);  // 16-weight chunks per decoder thread and stage
 };
 
 template <int BN, int OUT, bool BIAS, int QMODE, int SDT>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(448, 1)
     gemm_w4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
                    const void* __restrict__ s_rel, int64_t lds, const float* __restrict__ codebook,
                    const float* __restrict__ xs, const float* __restrict__ sch, const void* __restrict__ bias,
@@ -60,7 +61,7 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full[s], 1 + 4);
+      mbar_init(&full[s], 1 + C::DWARPS);
       mbar_init(&pkfull[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -77,7 +78,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
     for (int i = 0; i < 16; ++i) cb[i] = __ldg(codebook + i);
     if constexpr (SDT == H3B_FP8_E4M3) {
-      for (int b = threadIdx.x - 192; b < 256; b += 128) lut[b] = level_table(cb, fp8e4m3_to_f32(static_cast<uint32_t>(b)));
+      for (int b = threadIdx.x - 192; b < 256; b += 32 * C::DWARPS) lut[b] = level_table(cb, fp8e4m3_to_f32(static_cast<uint32_t>(b)));
     }
   }
   if (warp == 0 && lane == 0) {
@@ -173,9 +174,13 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive(&tempty[buf]);
     }
   } else {  // ----------------------------------------------------------------------------------- decoders
-    const int dt = threadIdx.x - 192;                 // 0 .. 127
+    const int dt = threadIdx.x - 192;                 // 0 .. 32 DWARPS - 1
     const int r_loc = (dt * C::CPT) >> 3;             // this thread's row of the B tile
     const int j0 = (dt * C::CPT) & 7;                 // its first 16-weight chunk in the row
+    struct Scales {
+      float g;                 // group-128 formats: the stage's one scale of this row
+      uint32_t f8[C::CPT];     // fp8 group 16: the scale byte of each chunk
+    };
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -186,29 +191,35 @@ __global__ void __launch_bounds__(320, 1)
       const bool row_ok = n < N;
       const unsigned char* srow = static_cast<const unsigned char*>(s_rel) +
                                   static_cast<int64_t>(row_ok ? n : 0) * lds * (SDT == H3B_FP8_E4M3 ? 1 : (SDT == H3B_FP32 ? 4 : 2));
-      for (int kb = 0; kb < num_kb; ++kb) {
-        // scales of this thread's chunks, loaded before the wait so their latency overlaps it
-        float s_g128 = 0.f;
-        uint32_t s_fp8[C::CPT];
+      // scales are global loads: they are issued two stages before they are used, so their latency hides behind the
+      // decode of the stages in between
+      auto load_scales = [&](int kb) {
+        Scales sc;
+        sc.g = 0.f;
         if constexpr (SDT == H3B_FP8_E4M3) {
 #pragma unroll
           for (int i = 0; i < C::CPT; ++i) {
             const int64_t e0 = static_cast<int64_t>(kb) * BK + 16 * (j0 + i);
-            s_fp8[i] = (row_ok && e0 < K) ? static_cast<uint32_t>(srow[e0 / GROUP]) : 0u;
+            sc.f8[i] = (row_ok && e0 < K) ? static_cast<uint32_t>(srow[e0 / GROUP]) : 0u;
           }
         } else {
+#pragma unroll
+          for (int i = 0; i < C::CPT; ++i) sc.f8[i] = 0u;
           const int64_t e0 = static_cast<int64_t>(kb) * BK + 16 * j0;
-          s_g128 = (row_ok && e0 < K) ? scale_at<SDT>(srow, e0 / GROUP) : 0.f;
+          sc.g = (row_ok && e0 < K) ? scale_at<SDT>(srow, e0 / GROUP) : 0.f;
         }
-        if (!mbar_wait(&pkfull[stage], phase, abort_flag)) { ok = false; break; }
+        return sc;
+      };
+      auto decode_stage = [&](const Scales& sc) -> bool {
+        if (!mbar_wait(&pkfull[stage], phase, abort_flag)) return false;
         uint4 t = make_uint4(0, 0, 0, 0);
-        if constexpr (SDT != H3B_FP8_E4M3) t = level_table(cb, s_g128);
+        if constexpr (SDT != H3B_FP8_E4M3) t = level_table(cb, sc.g);
         const unsigned char* prow = sP + stage * C::P_BYTES + r_loc * (BK / 2);
         unsigned char* brow = sB + stage * C::B_BYTES + r_loc * BK;
 #pragma unroll
         for (int i = 0; i < C::CPT; ++i) {
           const int j = j0 + i;
-          if constexpr (SDT == H3B_FP8_E4M3) t = lut[s_fp8[i]];
+          if constexpr (SDT == H3B_FP8_E4M3) t = lut[sc.f8[i]];
           const uint2 pk = *reinterpret_cast<const uint2*>(prow + 8 * j);
           const uint2 a = decode8(pk.x, t), b = decode8(pk.y, t);
           *reinterpret_cast<uint4*>(brow + ((j ^ (r_loc & 7)) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
@@ -217,6 +228,16 @@ __global__ void __launch_bounds__(320, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[stage]);
         if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        return true;
+      };
+      Scales s0 = load_scales(0), s1 = load_scales(1);
+      for (int kb = 0; kb < num_kb; kb += 2) {
+        const Scales s2 = load_scales(kb + 2);
+        if (!decode_stage(s0)) { ok = false; break; }
+        const Scales s3 = load_scales(kb + 3);
+        if (kb + 1 < num_kb && !decode_stage(s1)) { ok = false; break; }
+        s0 = s2;
+        s1 = s3;
       }
     }
   }
@@ -270,7 +291,7 @@ static int launch_w4(const int8_t* a, int64_t lda, const void* q4, int64_t ldq4,
   const int n_tiles = (N + BN - 1) / BN;
   int gn = static_cast<int>((24ll << 20) / (static_cast<int64_t>(BN) * K));
   gn = gn < 1 ? 1 : (gn > n_tiles ? n_tiles : gn);
-  kern<<<grid, 320, C::SMEM, st>>>(ta, tp, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, gn);
+  kern<<<grid, 192 + 32 * C::DWARPS, C::SMEM, st>>>(ta, tp, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, gn);
   return check_launch("gemm_w4_kernel");
 }
 
