@@ -738,7 +738,7 @@ def main():
     ap.add_argument("--workload", default="sweep", choices=WORKLOADS,
                     help="sweep: config 2 (default); block: config 3; stream: config 4; longseq: config 5")
     ap.add_argument("--store-dir", default="", help="stream workload: directory for the temporary ~7.9 GB h3t store")
-    ap.add_argument("--kv-exchange", default="ring", choices=["ring", "gather"],
+    ap.add_argument("--kv-exchange", default="gather", choices=["ring", "gather"],
                     help="block/longseq on several GPUs: key/value shards passed round a ring (overlapped) or all-gathered")
     args = ap.parse_args()
     args.ms = [int(v) for v in args.ms.split(",") if v]
