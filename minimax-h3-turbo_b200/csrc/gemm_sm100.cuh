@@ -28,11 +28,12 @@ constexpr int BK = 128;  // int8 elements (= bytes) of K per stage: one 128-byte
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+  static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 192 ? 5 : (BN >= 128 ? 6 : (BN >= 96 ? 7 : 8)));
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  // TMEM is allocated in power-of-two column counts (>= 32) holding two BN-column accumulators
+  static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;  // alignment slack + ring + barriers
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
 };
@@ -567,13 +568,24 @@ static bool pair_enabled() {
 }
 
 // Largest N tile that still gives every SM a tile; the smallest one otherwise.
+// N tile of a GEMM: 256 when 256-wide tiles give every SM work (the CTA-pair kernel's regime); otherwise the width that
+// minimises waves x width -- the time of the busiest SM -- so that small-M problems neither leave SMs idle nor run a
+// nearly empty last wave (wider on ties: fewer re-reads of A).
 static int pick_bn(int M, int N) {
   const int sms = num_sms();
-  const int mt = (M + BM - 1) / BM;
-  for (int bn : {256, 128, 64}) {
-    if (static_cast<int64_t>(mt) * ((N + bn - 1) / bn) >= sms) return bn;
+  const int64_t mt = (M + BM - 1) / BM;
+  if (mt * ((N + 255) / 256) >= sms) return 256;
+  int best = 32;
+  int64_t best_cost = -1;
+  for (int bn : {256, 192, 128, 96, 64, 32}) {
+    const int64_t tiles = mt * ((N + bn - 1) / bn);
+    const int64_t cost = ((tiles + sms - 1) / sms) * bn;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
   }
-  return 32;
+  return best;
 }
 
 template <int OUT, bool BIAS, int QMODE>
@@ -583,7 +595,9 @@ static int dispatch_bn(int bn, const int8_t* a, int64_t lda, const int8_t* b, in
     return launch_gemm_pair<OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
   switch (bn) {
     case 256: return launch_gemm<256, OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
+    case 192: return launch_gemm<192, OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
     case 128: return launch_gemm<128, OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
+    case 96: return launch_gemm<96, OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
     case 64: return launch_gemm<64, OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
     default: return launch_gemm<32, OUT, BIAS, QMODE>(a, lda, b, ldb, xs, sch, bias, out, ldo, M, N, K, st);
   }

@@ -19,20 +19,23 @@ namespace h3b {
 
 template <int BN>
 struct W4Cfg {
-  static constexpr int STAGES = BN >= 128 ? 4 : 6;
+  static constexpr int STAGES = BN >= 192 ? 4 : (BN >= 128 ? 4 : (BN >= 96 ? 5 : 6));
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int P_BYTES = BN * (BK / 2);
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + P_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int TMEM_COLS = GemmCfg<BN>::TMEM_COLS;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 4096 + 512;  // ring + fp8 level tables + barriers
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
-  static constexpr int DWARPS = 8;                 // decoder warps
+  // decoder warps: 8, or 6 when BN is a multiple of 96, so that a thread's CPT chunks (CPT dividing the 8 chunks
+  // of a row) lie in one row of the B tile
+  static constexpr int DWARPS = BN % 96 == 0 ? 6 : 8;
   static constexpr int CPT = BN * 8 / (32 * DWARPS);  // 16-weight chunks per decoder thread and stage
+  static_assert(CPT >= 1 && 8 % CPT == 0 && CPT * 32 * DWARPS == BN * 8, "decoder chunks must tile the rows");
 };
 
 template <int BN, int OUT, bool BIAS, int QMODE, int SDT>
-__global__ void __launch_bounds__(448, 1)
+__global__ void __launch_bounds__(192 + 32 * W4Cfg<BN>::DWARPS, 1)
     gemm_w4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
                    const void* __restrict__ s_rel, int64_t lds, const float* __restrict__ codebook,
                    const float* __restrict__ xs, const float* __restrict__ sch, const void* __restrict__ bias,
@@ -302,7 +305,7 @@ static bool w4_fused_ok(int64_t M, int64_t N, int64_t K, const void* q4, int64_t
                    ((s_dtype == H3B_FP16 || s_dtype == H3B_BF16 || s_dtype == H3B_FP32) && group == 128);
   if (!fmt || ldq4 % 16 || (reinterpret_cast<uintptr_t>(q4) & 15) || K % 16) return false;
   const int bn = pick_bn(static_cast<int>(M), static_cast<int>(N));
-  return bn <= 128 && M <= 1024;
+  return bn <= 192 && M <= 1024;
 }
 
 template <int OUT, bool BIAS, int QMODE, int SDT>
@@ -310,7 +313,9 @@ static int w4_dispatch_bn(int bn, const int8_t* a, int64_t lda, const void* q4, 
                           int64_t lds, const float* codebook, const float* xs, const float* sch, const void* bias, void* out,
                           int64_t ldo, int M, int N, int K, cudaStream_t st) {
   switch (bn) {
+    case 192: return launch_w4<192, OUT, BIAS, QMODE, SDT>(a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st);
     case 128: return launch_w4<128, OUT, BIAS, QMODE, SDT>(a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st);
+    case 96: return launch_w4<96, OUT, BIAS, QMODE, SDT>(a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st);
     case 64: return launch_w4<64, OUT, BIAS, QMODE, SDT>(a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st);
     default: return launch_w4<32, OUT, BIAS, QMODE, SDT>(a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st);
   }
