@@ -285,7 +285,10 @@ __global__ void __launch_bounds__(192, 1)
 //   tempty[b]  leader only: 2 x 128 epilogue threads (the peer's arrive remotely) have drained accumulator b
 constexpr int P_BN = 256;      // output columns per pair tile (N of the MMA)
 constexpr int P_BM = 2 * BM;   // output rows per pair tile
-constexpr int P_STAGES = 6;
+#ifndef H3B_PAIR_STAGES
+#define H3B_PAIR_STAGES 6  // build-time tuning knob: TMA/MMA ring depth of the CTA-pair kernel (7 measured the same)
+#endif
+constexpr int P_STAGES = H3B_PAIR_STAGES;
 constexpr int P_A_BYTES = BM * BK;           // this CTA's A half per stage
 constexpr int P_B_BYTES = (P_BN / 2) * BK;   // this CTA's B half per stage
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
