@@ -177,10 +177,15 @@ class ClockSampler:
 _CPU_WEIGHTS = {}
 
 
-def cpu_projection_times(projs, rows: int, reps: int = 1, seed: int = 0):
-    """The reference's CPU algorithm (oracle port) on a bounded sample: per (K, N) projection, one full weight decode (the
-    reference decodes on every call) plus quantise + exact int8 GEMM + epilogue on `rows` rows.  Returns
-    [(K, N, t_decode_s, t_per_row_s)]: the path is token-wise, so a call on M rows costs t_decode + M * t_per_row."""
+CPU_WEIGHT_ROWS = 1024  # output channels of each weight the CPU sample decodes and multiplies
+
+
+def cpu_projection_times(projs, rows: int, reps: int = 1, seed: int = 0, wrows: int = CPU_WEIGHT_ROWS):
+    """The reference's CPU algorithm (oracle port) on a bounded sample: per (K, N) projection, the weight decode (the
+    reference decodes on every call), the quantiser on `rows` tokens, and the exact int8 GEMM + epilogue of those tokens,
+    with the decode and the GEMM run on the first `wrows` output channels and scaled by N / wrows (both are linear in
+    N; the quantiser is not scaled).  Returns [(K, N, t_decode_s, t_per_row_s)]: the path is token-wise, so a call on M
+    rows costs t_decode + M * t_per_row."""
     sys.path.insert(0, str(ROOT))
     from oracle import qlinear_oracle as orc
 
@@ -190,18 +195,21 @@ def cpu_projection_times(projs, rows: int, reps: int = 1, seed: int = 0):
         if key not in _CPU_WEIGHTS:  # generated once per process, outside the timed part
             _CPU_WEIGHTS[key] = orc.synth_weight_int4_g128(n, k, seed=seed + k + n)
         q, s_rel, s_ch, cb = _CPU_WEIGHTS[key]
+        nr = min(n, wrows)
+        qs, ss, cs = q[:nr], s_rel[:nr], s_ch[:nr]
         x = orc.synth_activation(rows, k, seed=seed, outlier_frac=0.005)
         t_dec, t_rows = [], []
         for _ in range(reps):
             t0 = time.perf_counter()
-            grid = orc.decode_int8_grid(q, s_rel, "fp16", cb, 128)
+            grid = orc.decode_int8_grid(qs, ss, "fp16", cb, 128)
             t1 = time.perf_counter()
             codes, xs = orc.quantize_rows(x, "bf16")
-            acc = orc.int8_mm(codes, grid)
-            orc.epilogue(acc, xs, s_ch, None, "bf16")
             t2 = time.perf_counter()
-            t_dec.append(t1 - t0)
-            t_rows.append((t2 - t1) / rows)
+            acc = orc.int8_mm(codes, grid)
+            orc.epilogue(acc, xs, cs, None, "bf16")
+            t3 = time.perf_counter()
+            t_dec.append((t1 - t0) * n / nr)
+            t_rows.append(((t2 - t1) + (t3 - t2) * n / nr) / rows)
         res.append((k, n, min(t_dec), min(t_rows)))
     return res
 
@@ -245,8 +253,9 @@ def run_reference(args, rank):
             "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
             "config": config_dict(ms, args.gpus),
             "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": "port",
-                             "sample": f"{rows} rows per projection + one full weight decode per projection, per-token "
-                                       f"extrapolation to the sweep (numpy oracle of the reference CPU path, {cores} threads)",
+                             "sample": f"{rows} tokens and {CPU_WEIGHT_ROWS} output channels per projection (decode, quantise, "
+                                       f"int8 GEMM, epilogue), scaled per output channel and extrapolated per token to the "
+                                       f"sweep (numpy oracle of the reference CPU path, {cores} threads)",
                              "detail": detail},
             "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -293,7 +302,7 @@ def run_reference_dit(args):
             "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference", "config": cfg,
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": f"the four W4A8 linears only (attention, norms, RoPE excluded: an upper bound), "
-                                       f"{args.ref_rows} rows per projection + one full weight decode, per-token "
+                                       f"{args.ref_rows} tokens and {CPU_WEIGHT_ROWS} output channels per projection, scaled per channel, per-token "
                                        f"extrapolation to {tokens} tokens x {nb} blocks ({cores} threads)",
                              "detail": detail},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -535,7 +544,7 @@ def run_dit(args, rank, world, local):
         v, detail = cpu_block_rate(tokens, nb, args.cpu_rows)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"the four W4A8 linears only (attention, norms, RoPE excluded: an upper bound), {args.cpu_rows} "
-                         f"rows per projection + one full weight decode, per-token extrapolation ({cores} threads)",
+                         f"tokens and {CPU_WEIGHT_ROWS} output channels per projection, scaled per channel, per-token extrapolation ({cores} threads)",
                "detail": detail}
 
     rows = b - a
@@ -696,7 +705,7 @@ def run_stream(args, rank, world, local):
         v, detail = cpu_block_rate(tokens, nb, args.cpu_rows)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"the four W4A8 linears only (attention, norms excluded: an upper bound), {args.cpu_rows} rows per "
-                         f"projection + one full weight decode, per-token extrapolation to {nb} blocks ({cores} threads)",
+                         f"projection and {CPU_WEIGHT_ROWS} output channels, scaled per channel, per-token extrapolation to {nb} blocks ({cores} threads)",
                "detail": detail}
     cfgd = dict(cfgd, block_nbytes=nbytes, store_bytes=nb * nbytes, host_kinds=kinds, store_write_s=round(write_s, 1),
                 parallelism="one GPU")
@@ -957,8 +966,9 @@ def run_sweep(args, rank, world, local):
         cores = os.cpu_count() or 1
         v, detail = cpu_reference_rate(args.ms, args.cpu_rows)
         cpu = {"value": v, "unit": "TOPS", "cores": cores, "kind": "port",
-               "sample": f"{args.cpu_rows} rows per projection + one full weight decode per projection, per-token "
-                         f"extrapolation to the sweep (numpy oracle of the reference CPU path, {cores} threads)",
+               "sample": f"{args.cpu_rows} tokens and {CPU_WEIGHT_ROWS} output channels per projection (decode, quantise, "
+                         f"int8 GEMM, epilogue), scaled per output channel and extrapolated per token to the sweep "
+                         f"(numpy oracle of the reference CPU path, {cores} threads)",
                "detail": detail}
 
     if args.detail and rank == 0:
