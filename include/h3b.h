@@ -207,6 +207,11 @@ int h3b_streamer_stats(h3b_streamer* s, uint64_t* copies, uint64_t* bytes, doubl
 int h3b_host_register(void* ptr, size_t bytes, int read_only);
 int h3b_host_unregister(void* ptr);
 
+/* Self-test of the bounded-wait failure path (no reference counterpart): one thread waits on an mbarrier that nothing
+ * arrives on, gives up after limit_s (0 < limit_s <= 10) of GPU time, raises bit 0 of the device flag and writes 1 to
+ * *gave_up_device (device memory).  The context stays usable; read and clear the flag with h3b_device_error(1). */
+int h3b_selftest_wait_timeout(double limit_s, int* gave_up_device, void* stream);
+
 /* Device-side failure flag of the current device: a kernel whose bounded wait ran out sets it (and returns instead of
  * hanging).  Returns the flag and, when clear != 0, resets it.  Synchronises the device. */
 int h3b_device_error(int clear);

@@ -72,6 +72,7 @@ _SIGNATURES = {
     "h3b_host_register": ([_c_void_p, _sz, _int], _int),
     "h3b_host_unregister": ([_c_void_p], _int),
     "h3b_device_error": ([_int], _int),
+    "h3b_selftest_wait_timeout": ([ctypes.c_double, _c_void_p, _c_void_p], _int),
 }
 
 

@@ -113,11 +113,35 @@ static int noalloc_scratch(void** addr) {
   *addr = g_noalloc_addr[dev];
   return H3B_OK;
 }
+// The failure path of the bounded waits, exercised on purpose: one thread waits on an mbarrier that nothing arrives on;
+// after `limit_ns` of %globaltimer time it gives up, raises bit 0 of the device flag and returns (no trap, no fault).
+__global__ void wait_timeout_selftest_kernel(unsigned long long limit_ns, int* gave_up) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  mbar_fence_init();
+  const unsigned long long t0 = globaltimer_ns();
+  bool done = false;
+  for (uint32_t i = 0; !done; ++i) {
+    if (mbar_try_wait(&bar, 0)) break;
+    if ((i & 63) == 0 && globaltimer_ns() - t0 > limit_ns) {
+      atomicOr(&g_device_error, 1u);
+      *gave_up = 1;
+      done = true;
+    }
+  }
+}
 }  // namespace h3b
 
 using namespace h3b;
 
 extern "C" {
+
+int h3b_selftest_wait_timeout(double limit_s, int* gave_up_device, void* stream) {
+  if (!(limit_s > 0.0 && limit_s <= 10.0) || !gave_up_device) return fail(H3B_ERR_ARG, "selftest: limit must be in (0, 10] s");
+  wait_timeout_selftest_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<unsigned long long>(limit_s * 1e9), gave_up_device);
+  return check_launch("wait_timeout_selftest_kernel");
+}
 
 int h3b_version(void) { return H3B_ABI_VERSION; }
 

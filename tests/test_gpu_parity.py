@@ -302,3 +302,18 @@ def test_backends_report_b200():
 
 def test_no_device_error_was_raised():
     assert _lib.lib().h3b_device_error(1) == 0
+
+
+def test_a_bounded_wait_that_runs_out_reports_and_leaves_the_context_usable():
+    """Failure detection without a fault: a wait on a barrier nothing arrives on gives up after 0.2 s, raises the device
+    flag, and the next kernels run normally."""
+    L = _lib.lib()
+    assert L.h3b_device_error(1) == 0
+    gave_up = torch.zeros(1, dtype=torch.int32, device=DEV)
+    _lib.check(L.h3b_selftest_wait_timeout(0.2, gave_up.data_ptr(), _lib.stream_ptr(DEV)), "selftest")
+    assert L.h3b_device_error(1) == 1  # synchronises; then clears the flag
+    assert gave_up.item() == 1
+    a = torch.randint(-128, 128, (256, 512), device=DEV, dtype=torch.int8)
+    b = torch.randint(-127, 128, (384, 512), device=DEV, dtype=torch.int8)
+    assert torch.equal(ql._int8_mm(a, b).long(), (a.double() @ b.double().t()).long())
+    assert L.h3b_device_error(0) == 0
