@@ -27,8 +27,11 @@
 // bf16 significands (checked exhaustively), so one multiply suffices.  fp16: r and one Markstein correction
 // (q0 = RN(b r), e = b - q0 s exactly, q1 = RN(q0 + e r)) -- the correctly rounded quotient for every pair of fp16
 // operands (checked exhaustively).  fp32 activations use the IEEE division.
-// Rounding the dt quotient to an integer uses the fp32 magic constant 1.5 * 2^23 (round half-to-even), after clamping
-// at 127 in the dt domain; the int8 code is the low byte of the sum's bit pattern.
+// Rounding to dt uses the hardware round-to-nearest-even pack (cvt.rn.bf16x2.f32 / f16x2).  bf16 codes: the packed
+// quotient goes straight to integers (cvt.rni.s32.bf16, half-to-even) and a saturating byte pack (cvt.pack.sat.s8);
+// fp16 and fp32: the fp32 magic constant 1.5 * 2^23 rounds half-to-even after a clamp in the dt domain, and the code is
+// the low byte of the sum's bit pattern.
+#include <mutex>
 #include <type_traits>
 
 #include "h3b_common.cuh"
@@ -86,31 +89,38 @@ __device__ __forceinline__ uint32_t clamp_q2(uint32_t w) {
     return *reinterpret_cast<const uint32_t*>(&r);
   }
 }
-// Round two fp32 values to the nearest bf16 (ties to even), returned as fp32, on the FMA pipe: Veltkamp splitting with
-// C = 2^16 + 1 (g = v C, d = v - g, h = g + d; each step rounded once, never contracted).  Equal to round-to-nearest-even
-// for every fp32 significand whenever all intermediates are normal and finite, i.e. for |v| in [2^-125, 2^111) (checked
-// exhaustively by tests/test_numerics.py); callers use it only below 2^100 -- values under 2^-110 quantise to code 0
-// whatever their last bf16 bit.
-__device__ __forceinline__ float2 rne_bf16_fma(float2 v) {
-  const float2 g = __fmul2_rn(v, make_float2(65537.0f, 65537.0f));
-  const float2 d = __ffma2_rn(g, make_float2(-1.0f, -1.0f), v);
-  return __fadd2_rn(g, d);
-}
-constexpr float VELTKAMP_MAX = 1.2676506002282294e30f;  // 2^100
-
 // max(a, b, c), NaN operands ignored like fmaxf (one three-input instruction on sm_100)
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
 }
-// round half-to-even and saturate to [-128, 127]; the code in the low byte
-__device__ __forceinline__ uint32_t sat_s8(float v) {
-  int r;
-  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(v));
-  return static_cast<uint32_t>(r);
-}
 constexpr float RINT_MAGIC = 12582912.0f;  // 1.5 * 2^23: x + M rounds x to an integer (half-to-even) for |x| < 2^22
+
+// Codes of a bf16 pair of quotients (element 0 in the low half): each half rounded half-to-even to an integer
+// (cvt.rni.s32.bf16; NaN -> 0), saturated to [-128, 127] and packed as bytes: code0 | code1 << 8 | c << 16.
+__device__ __forceinline__ uint32_t codes2_bf16(uint32_t qb, uint32_t c) {
+  uint32_t d;
+  asm("{\n\t.reg .b16 lo, hi;\n\t.reg .s32 k0, k1;\n\tmov.b32 {lo, hi}, %1;\n\tcvt.rni.s32.bf16 k0, lo;\n\t"
+      "cvt.rni.s32.bf16 k1, hi;\n\tcvt.pack.sat.s8.s32.b32 %0, k1, k0, %2;\n\t}"
+      : "=r"(d) : "r"(qb), "r"(c));
+  return d;
+}
+// Codes of four elements given as the low (HI = false) or high halves of four bf16 pairs, the same rounding and
+// saturation: c0 | c1 << 8 | c2 << 16 | c3 << 24.
+#define H3B_CODES4_ASM(H)                                                                                     \
+  "{\n\t.reg .b16 a0, a1, a2, a3, b0, b1, b2, b3;\n\t.reg .s32 k0, k1, k2, k3, t;\n\t"                       \
+  "mov.b32 {a0, b0}, %1;\n\tmov.b32 {a1, b1}, %2;\n\tmov.b32 {a2, b2}, %3;\n\tmov.b32 {a3, b3}, %4;\n\t"      \
+  "cvt.rni.s32.bf16 k0, " H "0;\n\tcvt.rni.s32.bf16 k1, " H "1;\n\tcvt.rni.s32.bf16 k2, " H "2;\n\t"            \
+  "cvt.rni.s32.bf16 k3, " H "3;\n\tcvt.pack.sat.s8.s32.b32 t, k3, k2, 0;\n\tcvt.pack.sat.s8.s32.b32 %0, k1, k0, t;\n\t}"
+template <bool HI>
+__device__ __forceinline__ uint32_t codes4_bf16(uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3) {
+  uint32_t d;
+  if constexpr (HI) asm(H3B_CODES4_ASM("b") : "=r"(d) : "r"(p0), "r"(p1), "r"(p2), "r"(p3));
+  else asm(H3B_CODES4_ASM("a") : "=r"(d) : "r"(p0), "r"(p1), "r"(p2), "r"(p3));
+  return d;
+}
+#undef H3B_CODES4_ASM
 
 // silu(gate) * up in dt, as torch computes it: x / (1 + exp(-x)) in fp32, rounded to dt; the product of the two dt
 // values in fp32, rounded to dt.
@@ -137,16 +147,16 @@ __device__ __forceinline__ void load_raw(Raw<DT, SW>& raw, const void* x, int64_
   using RW = Raw<DT, SW>;
 #pragma unroll
   for (int l = 0; l < RW::L; ++l) {
-    const int64_t row = row0 + (SPLIT ? 0 : l);
+    // a row past the end reads the last row instead: its values only ever reach its own row group's scale slot and
+    // stores, which are skipped for rows past the end
+    const int64_t row = row0 + (SPLIT ? 0 : l) < M ? row0 + (SPLIT ? 0 : l) : M - 1;
     const int64_t c0 = col + (SPLIT ? l * (K / 2) : 0);
-    const bool valid = row < M;
-    const char* base = static_cast<const char*>(x) + static_cast<size_t>(valid ? row : 0) * static_cast<size_t>(ldx) * RW::ESZ;
+    const char* base = static_cast<const char*>(x) + static_cast<size_t>(row) * static_cast<size_t>(ldx) * RW::ESZ;
 #pragma unroll
     for (int h = 0; h < (SW ? 2 : 1); ++h) {
       const uint4* ptr = reinterpret_cast<const uint4*>(base + static_cast<size_t>(c0 + h * K) * RW::ESZ);
 #pragma unroll
-      for (int i = 0; i < RW::V16; ++i)
-        raw.u[(l * (SW ? 2 : 1) + h) * RW::V16 + i] = valid ? __ldg(ptr + i) : make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < RW::V16; ++i) raw.u[(l * (SW ? 2 : 1) + h) * RW::V16 + i] = __ldg(ptr + i);
     }
   }
 }
@@ -368,13 +378,8 @@ __global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __
             mB = max3f(mB, fabsf(v[i].y), fabsf(v[i + 1].y));
           }
         }
-        if (fmaxf(mA, mB) < VELTKAMP_MAX) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) b2[i] = rne_bf16_fma(v[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) b2[i] = unpack2<DT>(pack2<DT>(v[i]));
-        }
+        for (int i = 0; i < 16; ++i) b2[i] = unpack2<DT>(pack2<DT>(v[i]));
       } else {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -422,7 +427,7 @@ __global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __
         if (RG == 2 && row0 + 1 < M) xs_out[row0 + 1] = xsB;
       }
 
-      // ---- quantise: code = sat_s8(rint(dt(RN(b / s)))); cpair(i) = lane 0 code | lane 1 code << 8
+      // ---- quantise: code = sat(rint(dt(RN(b / s)))); cpair(i) = lane 0 code | lane 1 code << 8
       unsigned char* cbuf = reinterpret_cast<unsigned char*>(gbuf);  // G > 1: regroup area (the exchange is done)
       // (lane 0, lane 1) byte pairs by element e of the block; the 16 elements of chunk c at c * CSTRIDE bytes.
       // G = 16: register i is element t + 16 i (chunk i, slot t); G = 4: 16 (i >> 2) + 4 t + (i & 3).
@@ -454,15 +459,13 @@ __global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __
         for (int i = 0; i < 16; ++i) {
           const float2 b = b2[i];
           const float2 q0 = __fmul2_rn(b, R2);
-          float2 qd;
           if constexpr (DT == DT_BF16) {
-            // RNbf16(q0) is RNbf16(b / s); the saturating conversion rounds half-to-even and clamps to [-128, 127]
-            // (on the XU pipe, which the rest of the kernel leaves idle)
-            qd = rne_bf16_fma(q0);
-            put(i, __byte_perm(sat_s8(qd.x), sat_s8(qd.y), 0x0040));
+            // RNbf16(q0) is RNbf16(b / s) (the hardware pack rounds to nearest even); the codes round it half-to-even
+            // to an integer and saturate to [-128, 127]
+            put(i, codes2_bf16(pack2<DT>(q0), 0u));
           } else {
             const float2 e = __ffma2_rn(q0, nS2, b);
-            qd = unpack2<DT>(clamp_q2<DT>(pack2<DT>(__ffma2_rn(e, R2, q0))));  // dt(RN(b / s)), clamped
+            const float2 qd = unpack2<DT>(clamp_q2<DT>(pack2<DT>(__ffma2_rn(e, R2, q0))));  // dt(RN(b / s)), clamped
             const float2 rr = __fadd2_rn(qd, MG);  // rint, half-to-even
             put(i, __byte_perm(__float_as_uint(rr.x), __float_as_uint(rr.y), 0x0040));
           }
@@ -488,6 +491,229 @@ __global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __
       }
     }
   }
+}
+
+// ------------------------------------------------------------------------------------------------ warp-per-row kernel
+// bf16 activations, ConvRot 256, K a multiple of 512, quantise modes.  One warp owns a whole row.  Pass p transforms
+// chunk pair c = 32 p + lane (lane 0 at column 16 c, lane 1 at K/2 + 16 c) exactly as rotq_kernel's split mode does,
+// keeps dt(y) as bf16 pairs in the warp's row buffer in shared memory (64 bytes per thread per pass, so 2 K bytes per
+// row) and the running absmax in a register.  After the last pass a warp shuffle gives the row's amax, and a second
+// sweep over the buffer quantises and stores.  No CTA barrier: each warp runs its rows on its own, and the per-row
+// scalar work (the scale's division and reciprocal) is spread over the whole row instead of 32 elements per thread.
+// The same roundings as rotq_kernel (dt(y) is the hardware round-to-nearest-even pack), so the codes are identical.
+constexpr int ROWK_PASS = 1024;  // elements of a row per pass (32 threads x 2 lanes x 16)
+// The row kernel serves M >= ROWK_MIN_ROWS (below, a CTA per row spreads each row over more SMs) and rows whose buffer
+// leaves room for several warps per SM.
+#ifndef H3B_ROTQ_ROW_MIN_ROWS
+#define H3B_ROTQ_ROW_MIN_ROWS 4096
+#endif
+constexpr int64_t ROWK_MIN_ROWS = H3B_ROTQ_ROW_MIN_ROWS;
+constexpr size_t ROWK_MAX_WARP_BYTES = 16 * 1024;  // K <= 5120 (at 8192 and above the CTA kernel is faster)
+__host__ __device__ constexpr int rowk_xbytes() { return 2 * xgrp(16) * 8; }  // a warp's exchange area (two blocks)
+// Row buffer of a pass: per ConvRot block a 16 x 16 matrix of bf16 pairs (row i = elements 16 i .. 16 i + 15 of the
+// block), the four 16-byte chunks of row i stored in the order j ^ ((i >> 1) & 3), blocks 272 words apart: the
+// transform's column writes (16 threads, element t + 16 i) and the quantiser's row reads (thread t', 16-byte chunks of
+// row t') are both free of bank conflicts.
+constexpr int ROWK_BLOCK_WORDS = 16 * 16 + 16;
+__host__ __device__ inline size_t rowk_warp_bytes(int64_t K) {
+  return static_cast<size_t>((K + ROWK_PASS - 1) / ROWK_PASS) * (2 * ROWK_BLOCK_WORDS * 4) + rowk_xbytes();
+}
+__device__ __forceinline__ int rowk_word(int i, int col) { return 16 * i + 4 * ((col >> 2) ^ ((i >> 1) & 3)) + (col & 3); }
+
+template <int MODE, bool SW>
+__global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ x, int64_t ldx, int M, int K,
+                                                       int8_t* __restrict__ q, int64_t ldq, float* __restrict__ xs_out) {
+  constexpr int DT = DT_BF16;
+  constexpr float SCALE = 0.0625f;
+  extern __shared__ __align__(16) unsigned char rotq_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int P = (K + ROWK_PASS - 1) / ROWK_PASS;
+  const int nchunk = K / 32;  // chunk pairs per row; a multiple of 16, so a pass is full or its upper half-warp idles
+  unsigned char* wbase = rotq_smem + static_cast<size_t>(warp) * rowk_warp_bytes(K);
+  const int t = lane & 15;
+  // this half-warp's block in the row buffer of pass 0 (passes are 2 blocks apart)
+  uint32_t* bblk = reinterpret_cast<uint32_t*>(wbase + rowk_xbytes()) + (lane >> 4) * ROWK_BLOCK_WORDS;
+  float2* gbuf = reinterpret_cast<float2*>(wbase) + (lane >> 4) * xgrp(16);
+  const int64_t half = K / 2;
+  const int64_t rstep = static_cast<int64_t>(gridDim.x) * nw;
+  int64_t row = static_cast<int64_t>(blockIdx.x) * nw + warp;
+
+  Raw<DT, SW> raw;
+  auto load = [&](int64_t r, int p) {  // r < M; the idle half-warp of a row's last pass re-reads chunk nchunk - 1
+    const int c = 32 * p + lane;
+    load_raw<DT, SW, true>(raw, x, ldx, r, M, 16ll * (c < nchunk ? c : nchunk - 1), K);
+  };
+  // the four swizzled column offsets of this thread's element column t (row i uses colw[(i >> 1) & 3])
+  int colw[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) colw[j] = 4 * ((t >> 2) ^ j) + (t & 3);
+  int rowr[4];  // and the word offsets of the four 16-byte chunks of row t
+#pragma unroll
+  for (int j = 0; j < 4; ++j) rowr[j] = rowk_word(t, 4 * j);
+  if (row < M) load(row, 0);
+  for (; row < M; row += rstep) {
+    float mA = 0.f;
+    for (int p = 0; p < P; ++p) {
+      float2 v[16];
+      if constexpr (!SW) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const uint32_t wa[4] = {raw.u[i].x, raw.u[i].y, raw.u[i].z, raw.u[i].w};
+          const uint32_t wb[4] = {raw.u[2 + i].x, raw.u[2 + i].y, raw.u[2 + i].z, raw.u[2 + i].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 a = unpack2<DT>(wa[k]), b = unpack2<DT>(wb[k]);
+            v[8 * i + 2 * k] = make_float2(a.x, b.x);
+            v[8 * i + 2 * k + 1] = make_float2(a.y, b.y);
+          }
+        }
+      } else {
+        float f[16];
+        lane_f32<DT, SW>(raw, 0, f);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i].x = f[i];
+        lane_f32<DT, SW>(raw, 1, f);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i].y = f[i];
+      }
+      if (p + 1 < P) load(row, p + 1);
+      else if (row + rstep < M) load(row + rstep, 0);
+
+      // stage A (digits d0, d1 in registers), exchange, stage B (d2, d3 across the 16 threads of the block)
+#pragma unroll
+      for (int a = 0; a < 4; ++a) h4(v[4 * a], v[4 * a + 1], v[4 * a + 2], v[4 * a + 3], 1.0f);
+#pragma unroll
+      for (int d = 0; d < 4; ++d) h4(v[d], v[d + 4], v[d + 8], v[d + 12], 1.0f);
+      {
+        float4* wr = reinterpret_cast<float4*>(gbuf + t * XROW);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) wr[i] = make_float4(v[2 * i].x, v[2 * i].y, v[2 * i + 1].x, v[2 * i + 1].y);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = gbuf[j * XROW + t];
+        __syncwarp();
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a) h4(v[4 * a], v[4 * a + 1], v[4 * a + 2], v[4 * a + 3], 1.0f);
+#pragma unroll
+      for (int d = 0; d < 4; ++d) h4(v[d], v[d + 4], v[d + 8], v[d + 12], SCALE);
+
+      // dt(y) as bf16 pairs (lane 0 low, lane 1 high) into the row buffer; absmax of y (ck) or of dt(y) (eager)
+      uint32_t bw[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) bw[i] = pack2<DT>(v[i]);
+      float mP = 0.f;
+      if constexpr (MODE == MODE_CK) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) mP = max3f(mP, fabsf(v[i].x), fabsf(v[i].y));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 b = unpack2<DT>(bw[i]);
+          mP = max3f(mP, fabsf(b.x), fabsf(b.y));
+        }
+      }
+      if (32 * p + lane < nchunk) mA = fmaxf(mA, mP);
+      uint32_t* bp = bblk + p * (2 * ROWK_BLOCK_WORDS);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) bp[16 * i + colw[(i >> 1) & 3]] = bw[i];  // element t + 16 i: row i, column t
+    }
+    __syncwarp();  // the quantiser reads rows that other threads of the half-warp wrote
+
+    // the row's scale
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mA = fmaxf(mA, __shfl_xor_sync(0xffffffffu, mA, o));
+    const float xs = fmaxf(__fdiv_rn(mA, 127.0f), 1e-30f);
+    float s = round_dt<DT>(xs);
+    if (s == 0.f) s = tiny_dt<DT>();
+    if (lane == 0) xs_out[row] = xs;
+    const float r = __frcp_rn(s);
+    const float2 R2 = make_float2(r, r);
+
+    // quantise: code = sat(rint(dt(RN(b / s)))) with RNbf16(RN(b RN(1/s))) = RNbf16(RN(b / s)).  Thread t' takes row
+    // t' of its block, i.e. its own chunk pair c = 32 p + lane in element order, so its codes pack straight into words.
+    int8_t* qrow = q + row * ldq;
+    for (int p = 0; p < P; ++p) {
+      const uint32_t* bp = bblk + p * (2 * ROWK_BLOCK_WORDS);
+      uint32_t qb[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 u = *reinterpret_cast<const uint4*>(bp + rowr[j]);
+        qb[4 * j] = u.x; qb[4 * j + 1] = u.y; qb[4 * j + 2] = u.z; qb[4 * j + 3] = u.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) qb[e] = pack2<DT>(__fmul2_rn(unpack2<DT>(qb[e]), R2));
+      uint32_t wA[4], wB[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        wA[u] = codes4_bf16<false>(qb[4 * u], qb[4 * u + 1], qb[4 * u + 2], qb[4 * u + 3]);
+        wB[u] = codes4_bf16<true>(qb[4 * u], qb[4 * u + 1], qb[4 * u + 2], qb[4 * u + 3]);
+      }
+      const int c = 32 * p + lane;
+      if (c < nchunk) {
+        *reinterpret_cast<uint4*>(qrow + 16ll * c) = make_uint4(wA[0], wA[1], wA[2], wA[3]);
+        *reinterpret_cast<uint4*>(qrow + half + 16ll * c) = make_uint4(wB[0], wB[1], wB[2], wB[3]);
+      }
+    }
+  }
+}
+
+// H3B_ROTQ_ROW=0 in the environment keeps rotq_kernel for every shape (read once per process; for comparisons).
+static bool rowk_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("H3B_ROTQ_ROW");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// Warps per CTA for the row kernel: the most warps per SM that the row buffers allow (ties: more warps per CTA).
+// Chosen once per K and kept (a few entries; the device is the same kind on every call).
+struct RowkShape { int64_t K; int nw, ctas_per_sm, sms; };
+
+template <int MODE, bool SW>
+static int rowk_shape(int64_t K, RowkShape& out) {
+  static std::mutex mu;
+  static RowkShape cache[8];
+  static int n_cached = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_cached; ++i)
+    if (cache[i].K == K) { out = cache[i]; return 0; }
+  auto kern = rotq_row_kernel<MODE, SW>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rotq_row)");
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t per_warp = rowk_warp_bytes(K);
+  RowkShape best{K, 0, 0, sms};
+  for (int nw = 8; nw >= 1; --nw) {
+    const size_t smem = per_warp * nw;
+    if (smem > 227 * 1024) continue;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * nw, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(rotq_row)");
+    if (per_sm * nw > best.nw * best.ctas_per_sm) { best.nw = nw; best.ctas_per_sm = per_sm; }
+  }
+  if (best.nw == 0) return fail(H3B_ERR_UNSUPPORTED, "rotq_row: the row buffer does not fit in shared memory");
+  cache[n_cached < 8 ? n_cached++ : 7] = best;
+  out = best;
+  return 0;
+}
+
+template <int MODE, bool SW>
+static int rowk_launch(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, int64_t ldq, float* xs,
+                       cudaStream_t st) {
+  RowkShape sh;
+  if (int rc = rowk_shape<MODE, SW>(K, sh)) return rc;
+  const size_t smem = rowk_warp_bytes(K) * sh.nw;
+  const int64_t want = (M + sh.nw - 1) / sh.nw, cap = static_cast<int64_t>(sh.sms) * sh.ctas_per_sm;
+  const int blocks = static_cast<int>(want < cap ? want : cap);
+  rotq_row_kernel<MODE, SW><<<blocks, 32 * sh.nw, smem, st>>>(x, ldx, static_cast<int>(M), static_cast<int>(K), q, ldq,
+                                                                xs);
+  return check_launch("rotq_row_kernel");
 }
 
 // ------------------------------------------------------------------------------------------------ launcher
@@ -529,6 +755,10 @@ template <int DT, int CR, int MODE, bool SW>
 static int launch_split(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, int64_t ldq, float* xs, void* y,
                         int ydt, int64_t ldy, cudaStream_t st) {
   constexpr int G = CR >= 256 ? 16 : (CR == 64 ? 4 : 1);
+  if constexpr (DT == DT_BF16 && CR == 256 && MODE != MODE_ROTATE) {
+    if (K % 512 == 0 && M >= ROWK_MIN_ROWS && rowk_warp_bytes(K) <= ROWK_MAX_WARP_BYTES && rowk_enabled())
+      return rowk_launch<MODE, SW>(x, ldx, M, K, q, ldq, xs, st);
+  }
   if constexpr (DT != DT_FP32) {
     if (K % (32 * G) == 0 && K / 32 <= 512) return launch_t<DT, CR, MODE, SW, true>(x, ldx, M, K, q, ldq, xs, y, ydt, ldy, st);
   }
