@@ -419,14 +419,21 @@ class TimedLinear:
 
         self.ql, self.on, self.events, self.calls = ql, False, [], 0
 
+    def _run(self, x, w, input_act):
+        from minimax_h3_turbo_b200.h3 import block as blk
+
+        if isinstance(x, blk.Prenorm):  # qkv / fc1: RMSNorm + modulation fused into the quantiser
+            return blk.prenorm_linear(x, w)
+        return self.ql.linear(x, w, input_act=input_act)
+
     def __call__(self, x, w, input_act=None):
         import torch
 
         if not self.on:
-            return self.ql.linear(x, w, input_act=input_act)
+            return self._run(x, w, input_act)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        y = self.ql.linear(x, w, input_act=input_act)
+        y = self._run(x, w, input_act)
         e1.record()
         self.events.append((e0, e1))
         self.calls += 1
@@ -476,7 +483,7 @@ def run_dit(args, rank, world, local):
     x0 = torch.randn(tokens, HID, generator=gx, device=dev).to(torch.bfloat16)[a:b].contiguous()
     x = torch.empty_like(x0)
     lin = TimedLinear()
-    block = blk.DiTBlock(HEADS, HEAD_DIM, linear=lin, kv_exchange=args.kv_exchange)
+    block = blk.DiTBlock(HEADS, HEAD_DIM, linear=lin, kv_exchange=args.kv_exchange, fuse_norm=True)
     stream = torch.cuda.current_stream(dev)
 
     def forward(xin):

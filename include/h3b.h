@@ -95,6 +95,20 @@ int h3b_rms_modulate(const void* x, int x_dtype, int64_t ldx, int64_t M, int hid
                      const int32_t* segments, int n_segments, const int32_t* token_rows, void* h, int64_t ldh,
                      void* stream);
 
+/* RMSNorm + AdaLN modulation fused into the rotate+quantise kernel: the codes and scales of h = _scale_shift_(_rms(x))
+ * (model.py:64-66, 106-109, 239-241) without writing h; the activation side of the qkv and fc1 linears of a block.
+ * Bit-identical to h3b_rms_modulate (bf16) followed by h3b_rotq on its output.  Every tensor bf16:
+ *   x          [M, K], rows ldx elements apart; K a multiple of 512, at most 6144; convrot 256
+ *   w          [K] norm weight (the reference rounds it to x's dtype first)
+ *   shift      [n_rows, K] dt(shift);  scale1: [n_rows, K] dt(1 + dt(scale)), the factor _scale_shift_ multiplies by;
+ *              rows ldm elements apart
+ *   segments / token_rows as h3b_rms_modulate;  q [M, ldq] int8 codes, xs [M] fp32 scales as h3b_rotq
+ *   every device pointer 16-byte aligned */
+int h3b_rotq_rms_modulate(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w, float eps, const void* shift,
+                          const void* scale1, int64_t ldm, int64_t n_rows, const int32_t* segments, int n_segments,
+                          const int32_t* token_rows, int convrot, int quant_mode, int8_t* q, int64_t ldq, float* xs,
+                          void* stream);
+
 /* Gated residual update, in place: x = dt(x + other * dt(gate[row])) for tokens with a modulation row, others
  * unchanged.  Replaces _gate_ (model.py:111-115; torch's addcmul_, bit-identical).  Arguments as h3b_rms_modulate;
  * other: [M, hidden] of x_dtype, rows ldo elements apart. */

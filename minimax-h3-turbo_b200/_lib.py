@@ -36,6 +36,8 @@ _SIGNATURES = {
     "h3b_version": ([], _int),
     "h3b_last_error": ([], ctypes.c_char_p),
     "h3b_rotq": ([_c_void_p, _int, _i64, _i64, _i64, _int, _int, _int, _c_void_p, _i64, _c_void_p, _c_void_p], _int),
+    "h3b_rotq_rms_modulate": ([_c_void_p, _i64, _i64, _i64, _c_void_p, ctypes.c_float, _c_void_p, _c_void_p, _i64, _i64,
+                               _c_void_p, _int, _c_void_p, _int, _int, _c_void_p, _i64, _c_void_p, _c_void_p], _int),
     "h3b_rotate": ([_c_void_p, _int, _i64, _i64, _i64, _int, _c_void_p, _int, _i64, _c_void_p], _int),
     "h3b_qk_norm_rope": ([_c_void_p, _i64, _c_void_p, _i64, _int, _i64, _int, _int, _c_void_p, _c_void_p, _int,
                           ctypes.c_float, _c_void_p, _c_void_p, _i64, _int, _int, _c_void_p], _int),

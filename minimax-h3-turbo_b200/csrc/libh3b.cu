@@ -208,6 +208,43 @@ int h3b_rms_modulate(const void* x, int x_dtype, int64_t ldx, int64_t M, int hid
                              token_rows, h, ldh, static_cast<cudaStream_t>(stream));
 }
 
+int h3b_rotq_rms_modulate(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w, float eps, const void* shift,
+                          const void* scale1, int64_t ldm, int64_t n_rows, const int32_t* segments, int n_segments,
+                          const int32_t* token_rows, int convrot, int quant_mode, int8_t* q, int64_t ldq, float* xs,
+                          void* stream) {
+  if (M < 0 || K <= 0 || K % 512 || K > 6144)
+    return fail(H3B_ERR_ARG, "rotq_rms_modulate: K must be a positive multiple of 512, at most 6144");
+  if (convrot != 256) return fail(H3B_ERR_UNSUPPORTED, "rotq_rms_modulate: convrot must be 256");
+  if (quant_mode != H3B_QMODE_CK && quant_mode != H3B_QMODE_EAGER) return fail(H3B_ERR_ARG, "quant_mode must be 'ck' or 'eager'");
+  if (M == 0) return H3B_OK;
+  if (!x || !w || !q || !xs) return fail(H3B_ERR_ARG, "rotq_rms_modulate: null x, weight, codes or scales");
+  if (ldx < K || ldx % 8 || !aligned(x, 16) || !aligned(w, 16))
+    return fail(H3B_ERR_ARG, "rotq_rms_modulate: x / weight must be 16-byte aligned, x rows >= K elements apart, a multiple of 8");
+  if (ldq < K || ldq % 16 || !aligned(q, 16)) return fail(H3B_ERR_ARG, "q must be 16-byte aligned with a row stride >= K, multiple of 16");
+  if (n_segments < 0 || n_segments > H3B_MAX_SEGMENTS || (n_segments > 0 && !segments))
+    return fail(H3B_ERR_ARG, "rotq_rms_modulate: at most H3B_MAX_SEGMENTS segments, given as a host table");
+  const bool mod = n_segments > 0 || token_rows;
+  if (mod && (!shift || !scale1 || ldm < K || ldm % 8 || !aligned(shift, 16) || !aligned(scale1, 16)))
+    return fail(H3B_ERR_ARG, "rotq_rms_modulate: shift/scale1 must be 16-byte aligned rows of >= K, stride a multiple of 8");
+  RowNorm nrm{};
+  nrm.w = static_cast<const __nv_bfloat16*>(w);
+  nrm.shift = static_cast<const __nv_bfloat16*>(shift);
+  nrm.scale1 = static_cast<const __nv_bfloat16*>(scale1);
+  nrm.ldm = ldm;
+  nrm.eps = eps;
+  nrm.token_rows = token_rows;
+  nrm.segs.n = n_segments;
+  for (int i = 0; i < n_segments; ++i) {
+    if (segments[3 * i] < 0 || segments[3 * i + 1] < segments[3 * i] || segments[3 * i + 2] < 0 ||
+        segments[3 * i + 2] >= n_rows)
+      return fail(H3B_ERR_ARG, "rotq_rms_modulate: a segment has a negative bound, ends before it starts, or names a row >= n_rows");
+    nrm.segs.first[i] = segments[3 * i];
+    nrm.segs.end[i] = segments[3 * i + 1];
+    nrm.segs.row[i] = segments[3 * i + 2];
+  }
+  return rotq_rmsmod_launch(x, ldx, M, K, nrm, quant_mode, q, ldq, xs, static_cast<cudaStream_t>(stream));
+}
+
 int h3b_gate_residual(void* x, int x_dtype, int64_t ldx, const void* other, int64_t ldo, int64_t M, int hidden,
                       const void* gate, int64_t ldm, int64_t n_rows, int m_dtype, const int32_t* segments, int n_segments,
                       const int32_t* token_rows, void* stream) {

@@ -8,6 +8,7 @@
 //   tokens outside every segment keep n.
 // One CTA per row (persistent over rows): 16-byte loads, fp32 sum of squares per thread, warp shuffles and one shared
 // memory pass for the row total.  HBM-bound: 2 H bytes read + 2 H written per token (the modulation rows stay in L2).
+#pragma once
 #include "h3b_common.cuh"
 
 namespace h3b {

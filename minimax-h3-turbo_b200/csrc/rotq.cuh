@@ -35,6 +35,7 @@
 #include <type_traits>
 
 #include "h3b_common.cuh"
+#include "rmsmod.cuh"
 
 // Threads a CTA should at least have: row groups are added to a CTA until it reaches this (build-time tuning knob).
 #ifndef H3B_ROTQ_MIN_THREADS
@@ -520,9 +521,43 @@ __host__ __device__ inline size_t rowk_warp_bytes(int64_t K) {
 }
 __device__ __forceinline__ int rowk_word(int i, int col) { return 16 * i + 4 * ((col >> 2) ^ ((i >> 1) & 3)) + (col & 3); }
 
-template <int MODE, bool SW>
+// The fused prologue's operands (NORM): h = dt(dt(dt((x rs) w) s1) + sh) per token, rs = rsqrt(mean(x^2) + eps), the
+// steps and roundings of rms_modulate_warp_kernel (model.py:_rms :64-66, _scale_shift_ :106-109).  All bf16; scale1 is
+// dt(1 + dt(scale)), the factor _scale_shift_ multiplies by; a token outside every segment (row < 0) keeps n.
+struct RowNorm {
+  const __nv_bfloat16* w;       // [K]
+  const __nv_bfloat16* shift;   // [rows][ldm]
+  const __nv_bfloat16* scale1;  // [rows][ldm]
+  int64_t ldm;
+  float eps;
+  const int* token_rows;        // per-token modulation row (negative: none), or null: the segments decide
+  SegTable segs;
+};
+
+// 16 bf16 values from element e of a bf16 array (16-byte aligned) for lane 0 and from element e + off for lane 1, as
+// (lane 0, lane 1) pairs
+__device__ __forceinline__ void load_pairs16(const __nv_bfloat16* p, int64_t e, int64_t off, float2 (&out)[16]) {
+  const uint4* a = reinterpret_cast<const uint4*>(p + e);
+  const uint4* b = reinterpret_cast<const uint4*>(p + e + off);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint4 ua = __ldg(a + i), ub = __ldg(b + i);
+    const uint32_t wa[4] = {ua.x, ua.y, ua.z, ua.w}, wb[4] = {ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 fa = unpack2<DT_BF16>(wa[k]), fb = unpack2<DT_BF16>(wb[k]);
+      out[8 * i + 2 * k] = make_float2(fa.x, fb.x);
+      out[8 * i + 2 * k + 1] = make_float2(fa.y, fb.y);
+    }
+  }
+}
+__device__ __forceinline__ float2 rnd_bf16x2(float2 v) { return unpack2<DT_BF16>(pack2<DT_BF16>(v)); }
+
+template <int MODE, bool SW, bool NORM>
 __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ x, int64_t ldx, int M, int K,
-                                                       int8_t* __restrict__ q, int64_t ldq, float* __restrict__ xs_out) {
+                                                       int8_t* __restrict__ q, int64_t ldq, float* __restrict__ xs_out,
+                                                       const RowNorm nrm) {
+  static_assert(!(SW && NORM), "the norm prologue reads the block's residual stream, not a SwiGLU input");
   constexpr int DT = DT_BF16;
   constexpr float SCALE = 0.0625f;
   extern __shared__ __align__(16) unsigned char rotq_smem[];
@@ -553,6 +588,44 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
   if (row < M) load(row, 0);
   for (; row < M; row += rstep) {
     float mA = 0.f;
+    float2 RS2 = make_float2(0.f, 0.f);
+    int mrow = -1;
+    if constexpr (NORM) {
+      // sum of squares in rms_modulate_warp_kernel's order: lane l adds its 8-element vectors l, l + 32, ... in turn,
+      // then an xor-shuffle tree; the loads go out four vectors at a time
+      const uint4* xr = reinterpret_cast<const uint4*>(static_cast<const char*>(x) + row * ldx * 2);
+      const int vpw = K >> 8;
+      float ss = 0.f;
+      int v0 = 0;
+      for (; v0 + 4 <= vpw; v0 += 4) {
+        uint4 u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) u[j] = __ldg(xr + lane + 32 * (v0 + j));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float f[8];
+          unpack8<H3B_BF16>(u[j], f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ss = __fmaf_rn(f[i], f[i], ss);
+        }
+      }
+      for (; v0 < vpw; ++v0) {
+        float f[8];
+        unpack8<H3B_BF16>(__ldg(xr + lane + 32 * v0), f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = __fmaf_rn(f[i], f[i], ss);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), nrm.eps));
+      RS2 = make_float2(rs, rs);
+      if (nrm.token_rows) {
+        mrow = nrm.token_rows[row];
+      } else {
+        for (int s2 = 0; s2 < nrm.segs.n; ++s2)
+          if (row >= nrm.segs.first[s2] && row < nrm.segs.end[s2]) mrow = nrm.segs.row[s2];
+      }
+    }
     for (int p = 0; p < P; ++p) {
       float2 v[16];
       if constexpr (!SW) {
@@ -578,6 +651,21 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
       }
       if (p + 1 < P) load(row, p + 1);
       else if (row + rstep < M) load(row + rstep, 0);
+      if constexpr (NORM) {  // x -> h: n = dt((x rs) w); h = dt(dt(n s1) + sh) for a modulated token
+        const int64_t e = 16ll * ((32 * p + lane) < nchunk ? 32 * p + lane : nchunk - 1);
+        float2 a[16];
+        load_pairs16(nrm.w, e, half, a);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = rnd_bf16x2(__fmul2_rn(__fmul2_rn(v[i], RS2), a[i]));
+        if (mrow >= 0) {
+          load_pairs16(nrm.scale1 + mrow * nrm.ldm, e, half, a);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = rnd_bf16x2(__fmul2_rn(v[i], a[i]));
+          load_pairs16(nrm.shift + mrow * nrm.ldm, e, half, a);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = rnd_bf16x2(__fadd2_rn(v[i], a[i]));
+        }
+      }
 
       // stage A (digits d0, d1 in registers), exchange, stage B (d2, d3 across the 16 threads of the block)
 #pragma unroll
@@ -672,7 +760,7 @@ static bool rowk_enabled() {
 // Chosen once per K and kept (a few entries; the device is the same kind on every call).
 struct RowkShape { int64_t K; int nw, ctas_per_sm, sms; };
 
-template <int MODE, bool SW>
+template <int MODE, bool SW, bool NORM>
 static int rowk_shape(int64_t K, RowkShape& out) {
   static std::mutex mu;
   static RowkShape cache[8];
@@ -680,7 +768,7 @@ static int rowk_shape(int64_t K, RowkShape& out) {
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < n_cached; ++i)
     if (cache[i].K == K) { out = cache[i]; return 0; }
-  auto kern = rotq_row_kernel<MODE, SW>;
+  auto kern = rotq_row_kernel<MODE, SW, NORM>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rotq_row)");
   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -703,16 +791,16 @@ static int rowk_shape(int64_t K, RowkShape& out) {
   return 0;
 }
 
-template <int MODE, bool SW>
+template <int MODE, bool SW, bool NORM = false>
 static int rowk_launch(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, int64_t ldq, float* xs,
-                       cudaStream_t st) {
+                       cudaStream_t st, const RowNorm& nrm = RowNorm{}) {
   RowkShape sh;
-  if (int rc = rowk_shape<MODE, SW>(K, sh)) return rc;
+  if (int rc = rowk_shape<MODE, SW, NORM>(K, sh)) return rc;
   const size_t smem = rowk_warp_bytes(K) * sh.nw;
   const int64_t want = (M + sh.nw - 1) / sh.nw, cap = static_cast<int64_t>(sh.sms) * sh.ctas_per_sm;
   const int blocks = static_cast<int>(want < cap ? want : cap);
-  rotq_row_kernel<MODE, SW><<<blocks, 32 * sh.nw, smem, st>>>(x, ldx, static_cast<int>(M), static_cast<int>(K), q, ldq,
-                                                                xs);
+  rotq_row_kernel<MODE, SW, NORM><<<blocks, 32 * sh.nw, smem, st>>>(x, ldx, static_cast<int>(M), static_cast<int>(K), q,
+                                                                      ldq, xs, nrm);
   return check_launch("rotq_row_kernel");
 }
 
@@ -796,6 +884,17 @@ int rotq_launch(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, i
                   : launch_dt<MODE_CK, false>(x_dtype, convrot, x, ldx, M, K, q, ldq, xs, y, y_dtype, ldy, st);
   return swiglu ? launch_dt<MODE_EAGER, true>(x_dtype, convrot, x, ldx, M, K, q, ldq, xs, y, y_dtype, ldy, st)
                 : launch_dt<MODE_EAGER, false>(x_dtype, convrot, x, ldx, M, K, q, ldq, xs, y, y_dtype, ldy, st);
+}
+
+// RMSNorm + modulation fused into the quantiser (bf16 x, ConvRot 256, K a multiple of 512 and <= 6144: the shapes the
+// norm's warp-per-row kernel serves, whose sum order this reproduces).  Codes and scales are bit-identical to
+// rms_modulate_launch followed by rotq_launch on its output.
+int rotq_rmsmod_launch(const void* x, int64_t ldx, int64_t M, int64_t K, const RowNorm& nrm, int mode, int8_t* q,
+                       int64_t ldq, float* xs, cudaStream_t st) {
+  if (K % 512 || K > 6144) return fail(H3B_ERR_UNSUPPORTED, "rotq_rms_modulate: K must be a multiple of 512, at most 6144");
+  if (mode == MODE_CK) return rowk_launch<MODE_CK, false, true>(x, ldx, M, K, q, ldq, xs, st, nrm);
+  if (mode == MODE_EAGER) return rowk_launch<MODE_EAGER, false, true>(x, ldx, M, K, q, ldq, xs, st, nrm);
+  return fail(H3B_ERR_ARG, "rotq_rms_modulate: quant_mode must be ck or eager");
 }
 
 }  // namespace h3b

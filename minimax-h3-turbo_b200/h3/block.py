@@ -99,6 +99,73 @@ def rms_modulate(x: torch.Tensor, weight: torch.Tensor, eps: float, shift: torch
     return h
 
 
+class Prenorm:
+    """x with its block's RMSNorm + modulation still pending: h = scale_shift_(rms(x, weight, eps), shift, scale,
+    segments) (model.py:64-66, 106-109, 239-241).  The W4A8 linear that reads h takes it through the fused
+    norm + rotate + quantise kernel (prenorm_linear), so h never goes to memory; materialize() computes h."""
+
+    def __init__(self, x: torch.Tensor, weight: torch.Tensor, eps: float, shift: torch.Tensor, scale: torch.Tensor,
+                 segments: Sequence[Segment]):
+        self.x, self.weight, self.eps, self.shift, self.scale, self.segments = x, weight, eps, shift, scale, segments
+
+    @property
+    def shape(self):
+        return self.x.shape
+
+    @property
+    def dtype(self):
+        return self.x.dtype
+
+    @property
+    def device(self):
+        return self.x.device
+
+    def materialize(self) -> torch.Tensor:
+        return rms_modulate(self.x, self.weight, self.eps, self.shift, self.scale, self.segments)
+
+
+def prenorm_codes(pre: Prenorm, convrot: int = 256, quant_mode: str = "ck") -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
+    """(int8 codes [M, K], fp32 scales [M, 1]) of h = pre.materialize() from the fused kernel (h3b_rotq_rms_modulate),
+    bit-identical to quantising the materialised h; None where that kernel does not apply (not bf16 CUDA rows, K not a
+    multiple of 512 or above 6144, ConvRot other than 256)."""
+    x = pre.x
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] % 512 == 0 and x.shape[1] <= 6144
+            and convrot == 256):
+        return None
+    from .. import _lib
+
+    m, k = x.shape
+    x = _aligned_rows(x)
+    bf = torch.bfloat16
+    shift = pre.shift.to(bf)  # dt(shift[row]) and dt(1 + dt(scale[row])): what _scale_shift_ adds and multiplies by
+    scale1 = (1.0 + pre.scale.to(bf)).to(bf)
+    shift, scale1 = shift.contiguous(), scale1.contiguous()
+    if shift.shape != scale1.shape or shift.shape[-1] != k:
+        raise ValueError(f"shift / scale must be [rows, {k}], got {tuple(pre.shift.shape)} / {tuple(pre.scale.shape)}")
+    w = pre.weight.to(bf).contiguous()
+    n_rows = shift.shape[0]
+    table, n_seg, token_rows = _segment_args(pre.segments, m, n_rows, x.device)
+    q = torch.empty(m, k, dtype=torch.int8, device=x.device)
+    xs = torch.empty(m, 1, dtype=torch.float32, device=x.device)
+    L = _lib.lib()
+    _lib.check(L.h3b_rotq_rms_modulate(x.data_ptr(), m, k, x.stride(0), w.data_ptr(), float(pre.eps), shift.data_ptr(),
+                                       scale1.data_ptr(), shift.stride(0), n_rows, table, n_seg, _lib.ptr(token_rows),
+                                       convrot, _lib.QMODE[quant_mode], q.data_ptr(), k, xs.data_ptr(),
+                                       _lib.stream_ptr(x.device)), "rotq_rms_modulate")
+    return q, xs
+
+
+def prenorm_linear(pre: Prenorm, w, precision: str = "a8", quant_mode: str = "ck") -> torch.Tensor:
+    """linear(pre.materialize(), w) with the norm fused into the quantiser when it applies (W4A8 weight, a8)."""
+    if isinstance(w, ql.W4A8Weight) and precision == "a8" and pre.x.shape[0] > 0:
+        codes = prenorm_codes(pre, w.convrot, quant_mode)
+        if codes is not None:
+            if w.q.shape[1] * 2 != pre.x.shape[1]:
+                raise ValueError(f"input features {pre.x.shape[1]} do not match the weight's K={w.q.shape[1] * 2}")
+            return ql._gemm_codes(codes[0], codes[1], w, None, out_dtype=pre.x.dtype, quant_mode=quant_mode)
+    return ql.linear(pre.materialize(), w, precision=precision, quant_mode=quant_mode)
+
+
 def gate_(x: torch.Tensor, gate: torch.Tensor, other: torch.Tensor, segments: Sequence[Segment]) -> torch.Tensor:
     """x[a:b] += other[a:b] * gate[row] per segment, in place (model.py:111-115): the fused kernel for bf16/fp16 CUDA
     rows (bit-identical to torch's addcmul_), the reference's torch ops otherwise."""
@@ -250,7 +317,8 @@ class DiTBlock:
     forward: eight smaller attention calls and their merges cost more than the hidden transfers), so it is the default."""
 
     def __init__(self, heads: int, head_dim: int, norm_eps: float = 1e-5, qk_norm_eps: float = 1e-5,
-                 precision: str = "a8", attn_chunk: Optional[int] = None, linear=None, kv_exchange: str = "gather"):
+                 precision: str = "a8", attn_chunk: Optional[int] = None, linear=None, kv_exchange: str = "gather",
+                 fuse_norm: Optional[bool] = None):
         if kv_exchange not in ("ring", "gather"):
             raise ValueError(f"kv_exchange must be 'ring' or 'gather', got {kv_exchange!r}")
         self.kv_exchange = kv_exchange
@@ -259,12 +327,22 @@ class DiTBlock:
         self.attn_chunk = attn_chunk
         # the linear op: the W4A8 qlinear (default); tests of the token-sharding plumbing on CPU ranks pass a dense one
         self._linear = linear or (lambda x, w, input_act=None: ql.linear(x, w, precision=self.precision, input_act=input_act))
+        self._linear_is_default = linear is None
+        # RMSNorm + modulation fused into the quantiser of the qkv and fc1 linears: on for the default linear; a custom
+        # linear opts in with fuse_norm=True and then receives a Prenorm for those two
+        self._fuse_norm = linear is None if fuse_norm is None else fuse_norm
+
+    def _in_linear(self, h, w) -> torch.Tensor:
+        """The linear that reads the normalised stream (qkv, fc1): h is a tensor or a Prenorm."""
+        if isinstance(h, Prenorm) and self._linear_is_default:
+            return prenorm_linear(h, w, self.precision)
+        return self._linear(h, w)
 
     def attention(self, h: torch.Tensor, w: BlockWeights, cos: torch.Tensor, sin: torch.Tensor,
                   spec: Optional[ShardSpec] = None) -> torch.Tensor:
         s, heads, hd = h.shape[0], self.heads, self.head_dim
         inner = heads * hd
-        qkv = self._linear(h, w.qkv)
+        qkv = self._in_linear(h, w.qkv)
         q, k, v = (t.view(s, heads, hd) for t in qkv.split(inner, dim=-1))
         norm_rope_(q, k, w.q_norm, w.k_norm, self.qk_norm_eps, cos, sin)
         if spec is not None and spec.world > 1 and self.kv_exchange == "ring":
@@ -284,14 +362,15 @@ class DiTBlock:
         return self._linear(o, w.out)
 
     def mlp(self, h: torch.Tensor, w: BlockWeights) -> torch.Tensor:
-        return self._linear(self._linear(h, w.fc1), w.fc2, input_act="swiglu")
+        return self._linear(self._in_linear(h, w.fc1), w.fc2, input_act="swiglu")
 
     def __call__(self, x: torch.Tensor, w: BlockWeights, mod: Modulation, segments: Sequence[Segment], cos: torch.Tensor,
                  sin: torch.Tensor, spec: Optional[ShardSpec] = None) -> torch.Tensor:
         """x: [S_local, hidden] residual stream (updated in place and returned); cos/sin: [S_local, half] for these rows."""
-        h = rms_modulate(x, w.norm1, self.norm_eps, mod.shift_a, mod.scale_a, segments)
+        norm = Prenorm if self._fuse_norm else rms_modulate
+        h = norm(x, w.norm1, self.norm_eps, mod.shift_a, mod.scale_a, segments)
         gate_(x, mod.gate_a, self.attention(h, w, cos, sin, spec), segments)
-        h = rms_modulate(x, w.norm2, self.norm_eps, mod.shift_m, mod.scale_m, segments)
+        h = norm(x, w.norm2, self.norm_eps, mod.shift_m, mod.scale_m, segments)
         return gate_(x, mod.gate_m, self.mlp(h, w), segments)
 
 
