@@ -78,6 +78,8 @@ __device__ __forceinline__ uint32_t pack2(float2 v) {
     return *reinterpret_cast<const uint32_t*>(&h);
   }
 }
+__device__ __forceinline__ float2 rnd_bf16x2(float2 v) { return unpack2<DT_BF16>(pack2<DT_BF16>(v)); }
+
 // Packed clamp of the dt quotient before rounding.  bf16: |b / s| <= 127 (1 + 2^-8)^2 / (1 - 2^-24) < 128.5, so only
 // the top needs a clamp (rint(127.5) = 128 -> 127); fp16 also clamps at -128 (an overflowed fp16 rotation can reach it).
 template <int DT>
@@ -129,6 +131,21 @@ template <int DT>
 __device__ __forceinline__ float swiglu1(float g, float u) {
   const float sl = round_dt<DT>(g / (1.0f + expf(-g)));
   return round_dt<DT>(sl * u);
+}
+// The same for bf16, on (lane 0, lane 1) pairs.  silu's quotient matters only through its rounding to bf16, so it is
+// taken from __fdividef (within 2 ulp of g / d for d in [2^-126, 2^126]) unless that result lies within 4 ulp of a bf16
+// rounding midpoint (low 16 bits in [0x7FFC, 0x8004]) or g is outside (-87, 1e30) (d beyond 2^125, g infinite or NaN):
+// then both the approximation and the IEEE quotient RN(g / d) (within 0.5 ulp of g / d) round to the same bf16 value, or
+// the IEEE division is taken.  Every bf16 gate value is checked against torch's silu by tests/test_swiglu_gpu.py.
+__device__ __forceinline__ float silu_quot_bf16(float g, float d) {
+  float qt = __fdividef(g, d);
+  if (!(g > -87.0f && g < 1.0e30f) || ((__float_as_uint(qt) & 0xFFFFu) - 0x7FFCu) < 9u) qt = __fdiv_rn(g, d);
+  return qt;
+}
+__device__ __forceinline__ float2 swiglu2_bf16(float2 g, float2 u) {
+  const float2 d = __fadd2_rn(make_float2(1.0f, 1.0f), make_float2(expf(-g.x), expf(-g.y)));
+  const float2 sl = rnd_bf16x2(make_float2(silu_quot_bf16(g.x, d.x), silu_quot_bf16(g.y, d.y)));
+  return rnd_bf16x2(__fmul2_rn(sl, u));
 }
 
 // ------------------------------------------------------------------------------------------------ lanes
@@ -193,6 +210,34 @@ __device__ __forceinline__ void lane_f32(const Raw<DT, SW>& raw, int l, float (&
   if constexpr (SW) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = swiglu1<DT>(v[i], u[i]);
+  }
+}
+
+// Both lanes' 16 SwiGLU values as (lane 0, lane 1) pairs.  raw.u: lane 0 gate [0, 1], lane 0 up [2, 3], lane 1 gate
+// [4, 5], lane 1 up [6, 7] (16-bit activations).
+template <int DT>
+__device__ __forceinline__ void swiglu_lanes(const Raw<DT, true>& raw, float2 (&v)[16]) {
+  if constexpr (DT == DT_BF16) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint4 ga = raw.u[i], ua = raw.u[2 + i], gb = raw.u[4 + i], ub = raw.u[6 + i];
+      const uint32_t g0[4] = {ga.x, ga.y, ga.z, ga.w}, u0[4] = {ua.x, ua.y, ua.z, ua.w};
+      const uint32_t g1[4] = {gb.x, gb.y, gb.z, gb.w}, u1[4] = {ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 a = unpack2<DT>(g0[k]), b = unpack2<DT>(g1[k]), c = unpack2<DT>(u0[k]), e = unpack2<DT>(u1[k]);
+        v[8 * i + 2 * k] = swiglu2_bf16(make_float2(a.x, b.x), make_float2(c.x, e.x));
+        v[8 * i + 2 * k + 1] = swiglu2_bf16(make_float2(a.y, b.y), make_float2(c.y, e.y));
+      }
+    }
+  } else {
+    float f[16];
+    lane_f32<DT, true>(raw, 0, f);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i].x = f[i];
+    lane_f32<DT, true>(raw, 1, f);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i].y = f[i];
   }
 }
 
@@ -284,13 +329,7 @@ __global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __
         }
       }
     } else {
-      float f[16];
-      lane_f32<DT, SW>(raw, 0, f);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i].x = f[i];
-      lane_f32<DT, SW>(raw, 1, f);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i].y = f[i];
+      swiglu_lanes<DT>(raw, v);
     }
     if (gbase + gstep < ngroups) load_raw<DT, SW, SPLIT>(raw, x, ldx, (g + gstep) * RG, M, col, K);
 
@@ -551,7 +590,6 @@ __device__ __forceinline__ void load_pairs16(const __nv_bfloat16* p, int64_t e, 
     }
   }
 }
-__device__ __forceinline__ float2 rnd_bf16x2(float2 v) { return unpack2<DT_BF16>(pack2<DT_BF16>(v)); }
 
 template <int MODE, bool SW, bool NORM>
 __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ x, int64_t ldx, int M, int K,
@@ -641,13 +679,7 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
           }
         }
       } else {
-        float f[16];
-        lane_f32<DT, SW>(raw, 0, f);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i].x = f[i];
-        lane_f32<DT, SW>(raw, 1, f);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i].y = f[i];
+        swiglu_lanes<DT>(raw, v);
       }
       if (p + 1 < P) load(row, p + 1);
       else if (row + rstep < M) load(row + rstep, 0);
