@@ -483,7 +483,7 @@ def run_dit(args, rank, world, local):
     x0 = torch.randn(tokens, HID, generator=gx, device=dev).to(torch.bfloat16)[a:b].contiguous()
     x = torch.empty_like(x0)
     lin = TimedLinear()
-    block = blk.DiTBlock(HEADS, HEAD_DIM, linear=lin, kv_exchange=args.kv_exchange, fuse_norm=True)
+    block = blk.DiTBlock(HEADS, HEAD_DIM, linear=lin, kv_exchange=args.kv_exchange, fuse_norm=True, kv_groups=args.kv_groups)
     stream = torch.cuda.current_stream(dev)
 
     def forward(xin):
@@ -560,7 +560,8 @@ def run_dit(args, rank, world, local):
     fields = dit_common_fields(peaks(), lin_ops, lin.ms(), attn_flops, t_ms if world == 1 else t0.elapsed_time(t1), args.steps)
     if rank == 0:
         exch = "K/V shards passed round a ring of the ranks, overlapped with attention" if args.kv_exchange == "ring" \
-            else "K/V all-gather per block"
+            else (f"K/V all-gather per block in {args.kv_groups} head groups, each group's attention overlapping the later "
+                  "groups' gathers" if args.kv_groups > 1 else "K/V all-gather per block")
         cfg = dict(cfg, parallelism=f"token-shard x{world} (contiguous rows, {exch}, output all-gather)",
                    rows_per_rank=[e - s for s, e in (blk.shard_rows(tokens, world, r) for r in range(world))],
                    l2="inputs larger than L2 (each block streams ~0.6 GB of weights+activations per rank)")
@@ -569,9 +570,10 @@ def run_dit(args, rank, world, local):
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": cfg, **fields,
                 "linear_tops_whole_job": world * lin_ops * args.steps / (t_ms * 1e-3) / 1e12,
                 "output_finite": finite, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-                # per block: 4 W4A8 linears (rotate+quantise, decode, GEMM each), 2 RMSNorm+modulation, 1 q/k norm+RoPE,
-                # 2 gated residuals, and with the ring exchange one attention merge per key shard
-                "gpu_launches": 3 * lin.calls + (5 + (world if world > 1 and args.kv_exchange == "ring" else 0)) * nb * args.steps}
+                # per block: 4 W4A8 linears (rotate+quantise -- with the RMSNorm+modulation for qkv and fc1 --, decode,
+                # GEMM each), 1 q/k norm+RoPE, 2 gated residuals, and with the ring exchange one attention merge per key
+                # shard
+                "gpu_launches": 3 * lin.calls + (3 + (world if world > 1 and args.kv_exchange == "ring" else 0)) * nb * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -754,6 +756,7 @@ def main():
     ap.add_argument("--workload", default="sweep", choices=WORKLOADS,
                     help="sweep: config 2 (default); block: config 3; stream: config 4; longseq: config 5")
     ap.add_argument("--store-dir", default="", help="stream workload: directory for the temporary ~7.9 GB h3t store")
+    ap.add_argument("--kv-groups", type=int, default=4, help="block/longseq over several GPUs: head groups of the K/V all-gather")
     ap.add_argument("--kv-exchange", default="gather", choices=["ring", "gather"],
                     help="block/longseq on several GPUs: key/value shards passed round a ring (overlapped) or all-gathered")
     args = ap.parse_args()

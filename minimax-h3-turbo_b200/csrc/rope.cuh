@@ -37,11 +37,18 @@ __device__ __forceinline__ float ld_any(const void* p, int64_t i, int dt) {
   }
 }
 
+template <int TDT>  // the cos / sin tables' dtype, fixed per launch
+__device__ __forceinline__ float ld_tab(const void* p, int64_t i) {
+  if constexpr (TDT == H3B_BF16) return __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(p) + i));
+  else if constexpr (TDT == H3B_FP16) return __half2float(__ldg(static_cast<const __half*>(p) + i));
+  else return __ldg(static_cast<const float*>(p) + i);
+}
+
 constexpr int ROPE_WARPS = 8;
 
 // NI = D / 32 channels per lane; HPI heads of one token per warp item (their loads are issued together).
 // Items: (token, head group) of q, then of k.
-template <int DT, int NI, int HPI>
+template <int DT, int NI, int HPI, int TDT>
 __global__ void __launch_bounds__(32 * ROPE_WARPS) qk_norm_rope_kernel(
     void* __restrict__ q, int64_t ldq, void* __restrict__ k, int64_t ldk, int64_t S, int heads,
     const void* __restrict__ wq, const void* __restrict__ wk, int w_dtype, float eps, const void* __restrict__ cs,
@@ -100,8 +107,8 @@ __global__ void __launch_bounds__(32 * ROPE_WARPS) qk_norm_rope_kernel(
       float cv = 0.f, sv = 0.f;
       if (c < 2 * half) {
         const int j = c < half ? c : c - half;
-        cv = ld_any(cs, trow + j, t_dtype);
-        sv = ld_any(sn, trow + j, t_dtype);
+        cv = ld_tab<TDT>(cs, trow + j);
+        sv = ld_tab<TDT>(sn, trow + j);
       }
 #pragma unroll
       for (int hh = 0; hh < HPI; ++hh) {
@@ -127,7 +134,8 @@ static int qk_launch_d(void* q, int64_t ldq, void* k, int64_t ldk, int64_t S, in
   const int64_t want = (items + ROPE_WARPS - 1) / ROPE_WARPS;
   const int64_t cap = static_cast<int64_t>(sms) * 8;  // 8 resident 256-thread CTAs per SM
   const int blocks = static_cast<int>(want < cap ? want : cap);
-#define H3B_QKR(NI, HPI) qk_norm_rope_kernel<DT, NI, HPI><<<blocks, 32 * ROPE_WARPS, 0, st>>>(q, ldq, k, ldk, S, heads, wq, wk, w_dtype, eps, cs, sn, ldt, t_dtype, half)
+#define H3B_QKR_T(NI, HPI, TDT) qk_norm_rope_kernel<DT, NI, HPI, TDT><<<blocks, 32 * ROPE_WARPS, 0, st>>>(q, ldq, k, ldk, S, heads, wq, wk, w_dtype, eps, cs, sn, ldt, t_dtype, half)
+#define H3B_QKR(NI, HPI) do { if (t_dtype == H3B_BF16) H3B_QKR_T(NI, HPI, H3B_BF16); else if (t_dtype == H3B_FP16) H3B_QKR_T(NI, HPI, H3B_FP16); else H3B_QKR_T(NI, HPI, H3B_FP32); } while (0)
 #define H3B_QKR_H(NI) if (hpi == 4) H3B_QKR(NI, 4); else if (hpi == 2) H3B_QKR(NI, 2); else H3B_QKR(NI, 1)
   switch (D) {
     case 32: H3B_QKR_H(1); break;
@@ -138,6 +146,7 @@ static int qk_launch_d(void* q, int64_t ldq, void* k, int64_t ldk, int64_t S, in
   }
 #undef H3B_QKR_H
 #undef H3B_QKR
+#undef H3B_QKR_T
   return check_launch("qk_norm_rope_kernel");
 }
 

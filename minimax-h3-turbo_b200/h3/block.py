@@ -220,22 +220,36 @@ def shard_rows(total: int, world: int, rank: int) -> Tuple[int, int]:
 
 def gather_rows(x: torch.Tensor, spec: ShardSpec) -> torch.Tensor:
     """All-gather of row shards -> [total, ...] on every rank (NCCL all_gather of equal-size, padded buffers)."""
+    return gather_rows_async(x, spec)()
+
+
+def gather_rows_async(x: torch.Tensor, spec: ShardSpec):
+    """Starts gather_rows(x, spec) and returns a function that waits for it (on the caller's stream, for NCCL) and
+    returns the gathered rows: the collective runs while the caller queues other work."""
     if spec.group is None or spec.world == 1:
-        return x
+        return lambda: x
     import torch.distributed as dist
 
     sizes = [b - a for a, b in (shard_rows(spec.total, spec.world, r) for r in range(spec.world))]
     cap = max(sizes)
-    buf = torch.empty(cap, *x.shape[1:], dtype=x.dtype, device=x.device)
-    buf[: x.shape[0]] = x
+    if x.shape[0] == cap and x.is_contiguous():
+        buf = x
+    else:
+        buf = torch.empty(cap, *x.shape[1:], dtype=x.dtype, device=x.device)
+        buf[: x.shape[0]] = x
     out = torch.empty(spec.world * cap, *x.shape[1:], dtype=x.dtype, device=x.device)
     if dist.get_backend(spec.group) == "nccl":
-        dist.all_gather_into_tensor(out, buf, group=spec.group)
+        work = dist.all_gather_into_tensor(out, buf, group=spec.group, async_op=True)
     else:  # gloo (CPU ranks): list form
-        dist.all_gather(list(out.chunk(spec.world)), buf, group=spec.group)
-    if all(s == cap for s in sizes):
-        return out
-    return torch.cat([out[r * cap: r * cap + sizes[r]] for r in range(spec.world)])
+        work = dist.all_gather(list(out.chunk(spec.world)), buf, group=spec.group, async_op=True)
+
+    def finish() -> torch.Tensor:
+        work.wait()
+        if all(n == cap for n in sizes):
+            return out
+        return torch.cat([out[r * cap: r * cap + sizes[r]] for r in range(spec.world)])
+
+    return finish
 
 
 def attention_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -318,10 +332,15 @@ class DiTBlock:
 
     def __init__(self, heads: int, head_dim: int, norm_eps: float = 1e-5, qk_norm_eps: float = 1e-5,
                  precision: str = "a8", attn_chunk: Optional[int] = None, linear=None, kv_exchange: str = "gather",
-                 fuse_norm: Optional[bool] = None):
+                 fuse_norm: Optional[bool] = None, kv_groups: int = 4):
         if kv_exchange not in ("ring", "gather"):
             raise ValueError(f"kv_exchange must be 'ring' or 'gather', got {kv_exchange!r}")
+        if kv_groups < 1:
+            raise ValueError(f"kv_groups must be >= 1, got {kv_groups}")
         self.kv_exchange = kv_exchange
+        # "gather" over several ranks: the key/value all-gather goes in head groups, all started at once, and each
+        # group's attention runs as soon as its keys and values are in, while the later groups are still in flight
+        self.kv_groups = kv_groups
         self.heads, self.head_dim = heads, head_dim
         self.norm_eps, self.qk_norm_eps, self.precision = norm_eps, qk_norm_eps, precision
         self.attn_chunk = attn_chunk
@@ -348,6 +367,9 @@ class DiTBlock:
         if spec is not None and spec.world > 1 and self.kv_exchange == "ring":
             return self._linear(ring_attention(q, k, v, spec).reshape(s, inner), w.out)
         if spec is not None and spec.world > 1:  # every query needs every key and value
+            groups = self.kv_groups if heads % self.kv_groups == 0 and not (self.attn_chunk and self.attn_chunk < s) else 1
+            if groups > 1:
+                return self._linear(self._grouped_gather_attention(q, k, v, spec, groups), w.out)
             k = gather_rows(k.reshape(s, inner).contiguous(), spec).view(-1, heads, hd)
             v = gather_rows(v.reshape(s, inner).contiguous(), spec).view(-1, heads, hd)
         qh = q.transpose(0, 1).unsqueeze(0)
@@ -360,6 +382,27 @@ class DiTBlock:
             for a in range(0, s, step):
                 o[a:a + step] = F.scaled_dot_product_attention(qh[:, :, a:a + step], kh, vh)[0].transpose(0, 1).reshape(-1, inner)
         return self._linear(o, w.out)
+
+    def _grouped_gather_attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: ShardSpec,
+                                  groups: int) -> torch.Tensor:
+        """Attention of the local queries over all ranks' keys and values, gathered in `groups` head groups: every
+        group's K and V all-gathers are started first, then each group's attention waits only for its own."""
+        s, heads, hd = q.shape
+        hg = heads // groups
+        pending = []
+        for g in range(groups):
+            h0 = g * hg
+            kl = k[:, h0:h0 + hg].reshape(s, hg * hd).contiguous()
+            vl = v[:, h0:h0 + hg].reshape(s, hg * hd).contiguous()
+            pending.append((gather_rows_async(kl, spec), gather_rows_async(vl, spec)))
+        o = torch.empty(s, heads * hd, dtype=q.dtype, device=q.device)
+        for g, (kf, vf) in enumerate(pending):
+            h0 = g * hg
+            kg, vg = kf().view(-1, hg, hd), vf().view(-1, hg, hd)
+            qh = q[:, h0:h0 + hg].transpose(0, 1).unsqueeze(0)
+            kh, vh = (t.transpose(0, 1).unsqueeze(0) for t in (kg, vg))
+            o[:, h0 * hd:(h0 + hg) * hd] = F.scaled_dot_product_attention(qh, kh, vh)[0].transpose(0, 1).reshape(s, hg * hd)
+        return o
 
     def mlp(self, h: torch.Tensor, w: BlockWeights) -> torch.Tensor:
         return self._linear(self._in_linear(h, w.fc1), w.fc2, input_act="swiglu")

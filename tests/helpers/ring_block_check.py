@@ -1,5 +1,6 @@
 """Run by tests/test_block_gpu.py under torchrun (2 ranks, one GPU each): the token-sharded DiT block with the ring and
-the all-gather key/value exchanges against the unsharded block on rank 0's GPU.  Prints RING_OK / GATHER_OK."""
+the all-gather key/value exchanges (in head groups, and all at once) against the unsharded block on rank 0's GPU.
+Prints RING_OK / GATHER_OK / GATHER1_OK."""
 import os
 import sys
 from datetime import timedelta
@@ -39,8 +40,10 @@ def main():
         a, b = blk.shard_rows(S, world, rank)
         spec = blk.ShardSpec(a, b, S, dist.group.WORLD, world, rank)
         segs = [(max(s0, a) - a, min(s1, b) - a, r) for s0, s1, r in segs_full if min(s1, b) > max(s0, a)]
-        for mode in ("ring", "gather"):
-            y = blk.DiTBlock(HEADS, HD, kv_exchange=mode)(x[a:b].clone(), w, mod, segs, cos[a:b], sin[a:b], spec)
+        # gather: K/V all-gathered in 4 head groups (one head each here); gather1: all heads at once
+        for mode, exchange, groups in (("ring", "ring", 1), ("gather", "gather", 4), ("gather1", "gather", 1)):
+            block = blk.DiTBlock(HEADS, HD, kv_exchange=exchange, kv_groups=groups)
+            y = block(x[a:b].clone(), w, mod, segs, cos[a:b], sin[a:b], spec)
             full = blk.gather_rows(y, spec)
             upd, want = full.float() - x.float(), ref.float() - x.float()
             rel = ((upd - want).norm() / want.norm()).item()

@@ -144,7 +144,7 @@ def test_ring_block_on_two_gpus_equals_one_gpu():
     env = dict(__import__("os").environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert "RING_OK" in r.stdout and "GATHER_OK" in r.stdout, r.stdout[-3000:]
+    assert "RING_OK" in r.stdout and "GATHER_OK" in r.stdout and "GATHER1_OK" in r.stdout, r.stdout[-3000:]
 
 
 def test_fused_merge_kernel_equals_the_torch_merge():

@@ -1,5 +1,6 @@
 """Token sharding of the DiT block on CPU ranks (gloo, world size 2 and 3): the row split, the row all-gather and a
-sharded block -- K/V all-gathered, or passed round a ring with the attention merged by log-sum-exp; everything else
+sharded block -- K/V all-gathered (at once or in head groups), or passed round a ring with the attention merged by
+log-sum-exp; everything else
 token-wise -- equal the unsharded block.  The W4A8 linear is CUDA-only,
 so these ranks run the block with a dense fp32 linear; the GPU path swaps in the qlinear (tests/test_block_gpu.py)."""
 import os
@@ -52,7 +53,7 @@ def _segments(a, b):
     return out
 
 
-def _worker(rank, world, port, q, exchange):
+def _worker(rank, world, port, q, exchange, groups):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -61,7 +62,7 @@ def _worker(rank, world, port, q, exchange):
         spec = blk.ShardSpec(a, b, S, dist.group.WORLD, world, rank)
         g = blk.gather_rows(torch.arange(a, b, dtype=torch.float32).view(-1, 1), spec)
         ok_gather = torch.equal(g.view(-1), torch.arange(S, dtype=torch.float32))
-        block = blk.DiTBlock(HEADS, HD, linear=dense, kv_exchange=exchange)
+        block = blk.DiTBlock(HEADS, HD, linear=dense, kv_exchange=exchange, kv_groups=groups)
         y = block(x[a:b].clone(), w, mod, _segments(a, b), cos[a:b], sin[a:b], spec)
         full = blk.gather_rows(y, spec)
         q.put((rank, ok_gather, full))
@@ -69,14 +70,16 @@ def _worker(rank, world, port, q, exchange):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,exchange", [(2, "gather"), (3, "gather"), (2, "ring"), (3, "ring")])
-def test_sharded_block_equals_unsharded(world, exchange):
+@pytest.mark.parametrize("world,exchange,groups", [(2, "gather", 1), (3, "gather", 1), (2, "gather", 2), (3, "gather", 2),
+                                                  (2, "ring", 1), (3, "ring", 1)])
+def test_sharded_block_equals_unsharded(world, exchange, groups):
+    """groups = 2: the K/V all-gather in two head groups, both started before either group's attention."""
     x, w, mod, cos, sin = make_case()
     ref = blk.DiTBlock(HEADS, HD, linear=dense)(x.clone(), w, mod, _segments(0, S), cos, sin)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, exchange)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, exchange, groups)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=90) for _ in range(world)]
