@@ -52,3 +52,12 @@ def test_rejects_unsupported_shapes():
         rope.norm_rope_(q.float(), k.float(), wq, wk, 1e-5, cos, sin, impl="b200")
     with pytest.raises(ValueError):
         rope.norm_rope_(q, k, wq, wk, 1e-5, cos[:5], sin[:5], impl="b200")
+
+
+def test_k_only_with_fp32_weights_and_a_strided_layout():
+    qkv, q, k, wq, wk, cos, sin = _case(333, 8, 128, 48, torch.bfloat16, torch.float32, 7)
+    ref = qkv.clone()
+    rq, rk, _ = (t.view(333, 8, 128) for t in ref.split(1024, dim=-1))
+    rope.norm_rope_(None, rk, None, wk.float(), 1e-6, cos, sin, impl="torch")
+    rope.norm_rope_(None, k, None, wk.float(), 1e-6, cos, sin, impl="b200")
+    assert torch.equal(qkv, ref)
