@@ -756,7 +756,7 @@ def main():
     ap.add_argument("--workload", default="sweep", choices=WORKLOADS,
                     help="sweep: config 2 (default); block: config 3; stream: config 4; longseq: config 5")
     ap.add_argument("--store-dir", default="", help="stream workload: directory for the temporary ~7.9 GB h3t store")
-    ap.add_argument("--kv-groups", type=int, default=4, help="block/longseq over several GPUs: head groups of the K/V all-gather")
+    ap.add_argument("--kv-groups", type=int, default=1, help="block/longseq over several GPUs: head groups of the K/V all-gather")
     ap.add_argument("--kv-exchange", default="gather", choices=["ring", "gather"],
                     help="block/longseq on several GPUs: key/value shards passed round a ring (overlapped) or all-gathered")
     args = ap.parse_args()
