@@ -298,16 +298,6 @@ static int launch_w4(const int8_t* a, int64_t lda, const void* q4, int64_t ldq4,
   return check_launch("gemm_w4_kernel");
 }
 
-// Whether the decode-in-producer kernel takes this problem: few M tiles (the 1-CTA kernel's regime), a supported
-// weight format, and a packed weight TMA can read (16-byte aligned rows).
-static bool w4_fused_ok(int64_t M, int64_t N, int64_t K, const void* q4, int64_t ldq4, int s_dtype, int group) {
-  const bool fmt = (s_dtype == H3B_FP8_E4M3 && group == 16) ||
-                   ((s_dtype == H3B_FP16 || s_dtype == H3B_BF16 || s_dtype == H3B_FP32) && group == 128);
-  if (!fmt || ldq4 % 16 || (reinterpret_cast<uintptr_t>(q4) & 15) || K % 16) return false;
-  const int bn = pick_bn(static_cast<int>(M), static_cast<int>(N));
-  return bn <= 192 && M <= 1024;
-}
-
 template <int OUT, bool BIAS, int QMODE, int SDT>
 static int w4_dispatch_bn(int bn, const int8_t* a, int64_t lda, const void* q4, int64_t ldq4, const void* s_rel,
                           int64_t lds, const float* codebook, const float* xs, const float* sch, const void* bias, void* out,
@@ -321,35 +311,24 @@ static int w4_dispatch_bn(int bn, const int8_t* a, int64_t lda, const void* q4, 
   }
 }
 
-template <int OUT, bool BIAS, int QMODE>
-static int w4_dispatch_s(int s_dtype, int bn, const int8_t* a, int64_t lda, const void* q4, int64_t ldq4,
-                         const void* s_rel, int64_t lds, const float* codebook, const float* xs, const float* sch,
-                         const void* bias, void* out, int64_t ldo, int M, int N, int K, cudaStream_t st) {
-  switch (s_dtype) {
-    case H3B_FP8_E4M3: return w4_dispatch_bn<OUT, BIAS, QMODE, H3B_FP8_E4M3>(bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st);
-    case H3B_FP16: return w4_dispatch_bn<OUT, BIAS, QMODE, H3B_FP16>(bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st);
-    case H3B_BF16: return w4_dispatch_bn<OUT, BIAS, QMODE, H3B_BF16>(bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st);
-    default: return w4_dispatch_bn<OUT, BIAS, QMODE, H3B_FP32>(bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st);
-  }
-}
-
-int gemm_w4_launch(const int8_t* a, int64_t lda, const void* q4, int64_t ldq4, const void* s_rel, int s_dtype,
-                   int64_t lds, const float* codebook, const float* xs, const float* sch, const void* bias, void* out,
-                   int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, int qmode, cudaStream_t st) {
-  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
-  const int bn = pick_bn(m, n);
+// Every epilogue variant of the kernel for one scale dtype.  Each scale dtype is instantiated in its own translation
+// unit (k_w4_<dtype>.cu) so the units compile in parallel.
+template <int SDT>
+int w4_launch_sdt(int out_dtype, int qmode, int bn, const int8_t* a, int64_t lda, const void* q4, int64_t ldq4,
+                  const void* s_rel, int64_t lds, const float* codebook, const float* xs, const float* sch,
+                  const void* bias, void* out, int64_t ldo, int M, int N, int K, cudaStream_t st) {
   const bool b = bias != nullptr;
-#define H3B_W4(OUTT)                                                                                                     \
-  (qmode == H3B_QMODE_CK                                                                                                 \
-       ? (b ? w4_dispatch_s<OUTT, true, 0>(s_dtype, bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, m, n, k, st) \
-            : w4_dispatch_s<OUTT, false, 0>(s_dtype, bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, m, n, k, st)) \
-       : (b ? w4_dispatch_s<OUTT, true, 1>(s_dtype, bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, m, n, k, st) \
-            : w4_dispatch_s<OUTT, false, 1>(s_dtype, bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, m, n, k, st)))
+#define H3B_W4(OUTT)                                                                                                   \
+  (qmode == H3B_QMODE_CK                                                                                               \
+       ? (b ? w4_dispatch_bn<OUTT, true, 0, SDT>(bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st) \
+            : w4_dispatch_bn<OUTT, false, 0, SDT>(bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st)) \
+       : (b ? w4_dispatch_bn<OUTT, true, 1, SDT>(bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st) \
+            : w4_dispatch_bn<OUTT, false, 1, SDT>(bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, bias, out, ldo, M, N, K, st)))
   switch (out_dtype) {
     case H3B_BF16: return H3B_W4(OUT_BF16);
     case H3B_FP16: return H3B_W4(OUT_FP16);
     case H3B_FP32: return H3B_W4(OUT_FP32);
-    case H3B_INT32: return w4_dispatch_s<OUT_S32, false, 0>(s_dtype, bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, nullptr, out, ldo, m, n, k, st);
+    case H3B_INT32: return w4_dispatch_bn<OUT_S32, false, 0, SDT>(bn, a, lda, q4, ldq4, s_rel, lds, codebook, xs, sch, nullptr, out, ldo, M, N, K, st);
     default: return fail(H3B_ERR_ARG, "out dtype must be bf16, fp16, fp32 or int32");
   }
 #undef H3B_W4

@@ -22,9 +22,20 @@ int cuda_fail(cudaError_t e, const char* what);
 int check_launch(const char* what);
 
 // ----------------------------------------------------------------------------------------------- device failure flag
-// Bit 0: an mbarrier wait timed out.  Bit 1: a kernel saw an impossible configuration.
-// (libh3b.so is one translation unit, so the flag is defined here, once.)
-__device__ unsigned int g_device_error = 0;
+// Bit 0: an mbarrier wait timed out.  Bit 1: a kernel saw an impossible configuration.  Every translation unit of
+// libh3b.so has its own copy (internal linkage, no relocatable device code); H3B_DEVICE_ERROR_ACCESSOR defines the
+// unit's host function that reads (and optionally clears) it, and h3b_device_error ORs them all.
+static __device__ unsigned int g_device_error = 0;
+
+#define H3B_DEVICE_ERROR_ACCESSOR(name)                                                 \
+  cudaError_t name(unsigned* v, int clear) {                                            \
+    cudaError_t e = cudaMemcpyFromSymbol(v, g_device_error, sizeof(unsigned));          \
+    if (e == cudaSuccess && clear) {                                                    \
+      const unsigned zero = 0;                                                          \
+      e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(unsigned));                  \
+    }                                                                                   \
+    return e;                                                                           \
+  }
 
 constexpr unsigned long long H3B_WAIT_LIMIT_NS = 2000000000ull;  // 2 s of GPU time per wait
 

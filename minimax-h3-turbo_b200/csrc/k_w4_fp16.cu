@@ -1,0 +1,12 @@
+// Translation unit: the decode-in-producer W4A8 GEMM (gemm_w4.cuh) for fp16 group scales, every epilogue variant.
+#include "gemm_w4.cuh"
+
+namespace h3b {
+
+template int w4_launch_sdt<H3B_FP16>(int, int, int, const int8_t*, int64_t, const void*, int64_t, const void*, int64_t,
+                                  const float*, const float*, const float*, const void*, void*, int64_t, int, int, int,
+                                  cudaStream_t);
+
+H3B_DEVICE_ERROR_ACCESSOR(device_error_w4_fp16)
+
+}  // namespace h3b

@@ -1,5 +1,5 @@
-// libh3b.so: the C ABI declared in include/h3b.h, argument validation, error state, and the kernels (one translation
-// unit, so the device failure flag is a single symbol shared by every kernel).
+// libh3b.so: the C ABI declared in include/h3b.h, argument validation and error state, the block streamer and the
+// wait self-test.  The kernels live in the k_*.cu translation units (launch.h lists what each exports).
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -27,13 +27,7 @@ int check_launch(const char* what) {
 
 }  // namespace h3b
 
-#include "attn_merge.cuh"
-#include "decode.cuh"
-#include "gemm_sm100.cuh"
-#include "gemm_w4.cuh"
-#include "rmsmod.cuh"
-#include "rope.cuh"
-#include "rotq.cuh"
+#include "launch.h"
 #include "streamer.cuh"
 
 namespace h3b {
@@ -130,6 +124,7 @@ __global__ void wait_timeout_selftest_kernel(unsigned long long limit_ns, int* g
     }
   }
 }
+static H3B_DEVICE_ERROR_ACCESSOR(device_error_abi)
 }  // namespace h3b
 
 using namespace h3b;
@@ -212,7 +207,7 @@ int h3b_rotq_rms_modulate(const void* x, int64_t M, int64_t K, int64_t ldx, cons
                           const void* scale1, int64_t ldm, int64_t n_rows, const int32_t* segments, int n_segments,
                           const int32_t* token_rows, int convrot, int quant_mode, int8_t* q, int64_t ldq, float* xs,
                           void* stream) {
-  if (M < 0 || K <= 0 || K % 512 || K > 6144)
+  if (M < 0 || K <= 0 || !rotq_rmsmod_supported(K))
     return fail(H3B_ERR_ARG, "rotq_rms_modulate: K must be a positive multiple of 512, at most 6144");
   if (convrot != 256) return fail(H3B_ERR_UNSUPPORTED, "rotq_rms_modulate: convrot must be 256");
   if (quant_mode != H3B_QMODE_CK && quant_mode != H3B_QMODE_EAGER) return fail(H3B_ERR_ARG, "quant_mode must be 'ck' or 'eager'");
@@ -326,7 +321,7 @@ int h3b_w4a8_gemm(const int8_t* qa, int64_t lda, const float* xs, int64_t M, con
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (w4_fused_ok(M, N, K, q4, ldq4, s_dtype, group))  // few M tiles: decode inside the GEMM's producer warps
     return gemm_w4_launch(qa, lda, q4, ldq4, s_rel, s_dtype, lds, codebook, xs, s_ch, bias, out, out_dtype, ldo, M, N, K,
-                          quant_mode, st);
+                          quant_mode, workspace, ws_bytes, st);
   int8_t* grid = static_cast<int8_t*>(workspace);
   rc = decode_launch(q4, N, K, ldq4, s_rel, s_dtype, lds, codebook, group, grid, K, st);
   if (rc) return rc;
@@ -579,12 +574,14 @@ int h3b_device_error(int clear) {
   unsigned int v = 0;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return -static_cast<int>(cuda_fail(e, "cudaDeviceSynchronize"));
-  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
-  if (e != cudaSuccess) return -static_cast<int>(cuda_fail(e, "cudaMemcpyFromSymbol"));
-  if (clear) {
-    const unsigned int zero = 0;
-    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
-    if (e != cudaSuccess) return -static_cast<int>(cuda_fail(e, "cudaMemcpyToSymbol"));
+  cudaError_t (*const units[])(unsigned*, int) = {device_error_abi, device_error_act, device_error_decode,
+                                                  device_error_gemm, device_error_w4, device_error_w4_fp8,
+                                                  device_error_w4_fp16, device_error_w4_bf16, device_error_w4_fp32};
+  for (auto unit : units) {
+    unsigned u = 0;
+    e = unit(&u, clear);
+    if (e != cudaSuccess) return -static_cast<int>(cuda_fail(e, "device failure flag"));
+    v |= u;
   }
   return static_cast<int>(v);
 }

@@ -10,6 +10,7 @@
 // memory pass for the row total.  HBM-bound: 2 H bytes read + 2 H written per token (the modulation rows stay in L2).
 #pragma once
 #include "h3b_common.cuh"
+#include "launch.h"
 
 namespace h3b {
 
@@ -67,13 +68,6 @@ __device__ __forceinline__ void load8(const void* p, int64_t e, int dt, float (&
   }
 }
 
-// Token segments passed by value (no device table to upload per call).
-constexpr int MAX_SEGMENTS = H3B_MAX_SEGMENTS;
-struct SegTable {
-  int n;
-  int64_t first[MAX_SEGMENTS], end[MAX_SEGMENTS];
-  int row[MAX_SEGMENTS];
-};
 
 // VPT = 8-element vectors per thread; blockDim.x * VPT * 8 >= H.  The modulation row of token r is token_rows[r] when
 // that map is given (negative: none), else the row of the segment holding r.

@@ -45,7 +45,6 @@
 namespace h3b {
 
 enum { DT_BF16 = 0, DT_FP16 = 1, DT_FP32 = 2 };
-enum { MODE_CK = 0, MODE_EAGER = 1, MODE_ROTATE = 2 };
 
 // ------------------------------------------------------------------------------------------------ dtype helpers
 template <int DT>
@@ -560,18 +559,6 @@ __host__ __device__ inline size_t rowk_warp_bytes(int64_t K) {
 }
 __device__ __forceinline__ int rowk_word(int i, int col) { return 16 * i + 4 * ((col >> 2) ^ ((i >> 1) & 3)) + (col & 3); }
 
-// The fused prologue's operands (NORM): h = dt(dt(dt((x rs) w) s1) + sh) per token, rs = rsqrt(mean(x^2) + eps), the
-// steps and roundings of rms_modulate_warp_kernel (model.py:_rms :64-66, _scale_shift_ :106-109).  All bf16; scale1 is
-// dt(1 + dt(scale)), the factor _scale_shift_ multiplies by; a token outside every segment (row < 0) keeps n.
-struct RowNorm {
-  const __nv_bfloat16* w;       // [K]
-  const __nv_bfloat16* shift;   // [rows][ldm]
-  const __nv_bfloat16* scale1;  // [rows][ldm]
-  int64_t ldm;
-  float eps;
-  const int* token_rows;        // per-token modulation row (negative: none), or null: the segments decide
-  SegTable segs;
-};
 
 // 16 bf16 values from element e of a bf16 array (16-byte aligned) for lane 0 and from element e + off for lane 1, as
 // (lane 0, lane 1) pairs
@@ -921,9 +908,11 @@ int rotq_launch(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, i
 // RMSNorm + modulation fused into the quantiser (bf16 x, ConvRot 256, K a multiple of 512 and <= 6144: the shapes the
 // norm's warp-per-row kernel serves, whose sum order this reproduces).  Codes and scales are bit-identical to
 // rms_modulate_launch followed by rotq_launch on its output.
+bool rotq_rmsmod_supported(int64_t K) { return K > 0 && K % 512 == 0 && K <= 6144; }
+
 int rotq_rmsmod_launch(const void* x, int64_t ldx, int64_t M, int64_t K, const RowNorm& nrm, int mode, int8_t* q,
                        int64_t ldq, float* xs, cudaStream_t st) {
-  if (K % 512 || K > 6144) return fail(H3B_ERR_UNSUPPORTED, "rotq_rms_modulate: K must be a multiple of 512, at most 6144");
+  if (!rotq_rmsmod_supported(K)) return fail(H3B_ERR_UNSUPPORTED, "rotq_rms_modulate: K must be a multiple of 512, at most 6144");
   if (mode == MODE_CK) return rowk_launch<MODE_CK, false, true>(x, ldx, M, K, q, ldq, xs, st, nrm);
   if (mode == MODE_EAGER) return rowk_launch<MODE_EAGER, false, true>(x, ldx, M, K, q, ldq, xs, st, nrm);
   return fail(H3B_ERR_ARG, "rotq_rms_modulate: quant_mode must be ck or eager");
