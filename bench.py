@@ -18,7 +18,13 @@ with no data-path collective ("scaling": "weak"); the time is the max over ranks
   cpu_baseline  the oracle (a numpy restatement of the reference's CPU qlinear) on a bounded row sample, all host
             cores, extrapolated per token (the path is token-wise) to the same sweep
 
-`--impl reference` runs only the reference's CPU algorithm (the oracle port) on rank 0 and prints its line.
+  sharded_block  BASELINE config 5 (59440 tokens, 4 W4A8 DiT blocks) token-sharded over the N ranks: tokens/s, ms per
+            forward, the W4A8 linears / attention / exposed key-value exchange per forward, NCCL ranks, and (N > 1) a
+            check of 256 gathered rows against the whole sequence recomputed on rank 0 alone
+  block     (N = 1) BASELINE config 3: one DiT block on 12290 tokens, tokens/s
+
+`--impl reference` runs the reference's own CPU qlinear (staged under oracle/_ref by oracle/make_ref.py; the numpy port
+of it when absent) on rank 0, and times the reference's portable CUDA path beside it.
 """
 from __future__ import annotations
 
@@ -37,7 +43,8 @@ SWEEP = [(5120, 5120), (5120, 13824), (13824, 5120)]  # (K, N)
 MS = [256, 2048, 16384, 65536]
 METRIC = "W4A8 qlinear int8 TOPS"
 WORKLOADS = ("sweep", "block", "stream", "longseq")
-GEMM_DRAM_BYTES_PER_OP = 349.907712e6 / (2.0 * 16384 * 5120 * 5120)
+# (K, N, M) -> DRAM bytes read + written by that point's GEMM launch (ncu, one capture of the sweep's launches)
+GEMM_DRAM_BYTES = {}
 HID, HEADS, HEAD_DIM, FFN = 5120, 40, 128, 13824  # DiT width, attention heads x head dim, SwiGLU width
 BLOCK_LINEARS = [(HID, 3 * HID), (HID, HID), (HID, 2 * FFN), (FFN, HID)]  # (K, N): qkv, out, fc1, fc2 (SwiGLU input)
 BLOCK_OPS_PER_TOKEN = sum(2.0 * k * n for k, n in BLOCK_LINEARS)  # 634.4 M
@@ -233,31 +240,178 @@ def cpu_block_rate(tokens: int, n_blocks: int, rows: int):
     return tokens / total_t, detail
 
 
+def load_reference():
+    """The reference's own qlinear module (h3turbo/h3/qlinear.py, unchanged) staged under oracle/_ref/ by
+    oracle/make_ref.py, or None when it has not been staged."""
+    import importlib
+
+    ref = ROOT / "oracle" / "_ref"
+    if not (ref / "h3turbo" / "h3" / "qlinear.py").is_file():
+        return None
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    ql = importlib.import_module("h3turbo.h3.qlinear")
+    types = importlib.import_module("h3turbo.h3.types")
+    return ql, types
+
+
+def reference_weight(types, k, n, seed, device):
+    """The benchmark's int4 group-128 weight (the oracle's seeded generator) as the reference's own W4A8Weight."""
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import qlinear_oracle as orc
+
+    q, s_rel, s_ch, cb = orc.synth_weight_int4_g128(n, k, seed=seed)
+    return types.W4A8Weight(torch.from_numpy(q).to(device), torch.from_numpy(s_rel).to(device),
+                            torch.from_numpy(s_ch).to(device), torch.from_numpy(cb).to(device), 128, 256)
+
+
+def reference_activation(m, k, seed, device):
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import qlinear_oracle as orc
+
+    bits = orc.synth_activation(m, k, seed=seed, outlier_frac=0.005)
+    return torch.from_numpy(bits.view("int16").copy()).view(torch.bfloat16).to(device)
+
+
+def reference_cuda_rate(ql, types, ms, reps=1):
+    """TOPS of the reference's own portable CUDA path -- qlinear.linear(..., backend="torch"): its cuBLAS rotation,
+    "ck" quantiser, per-call int8 grid decode and torch._int_mm (cuBLASLt), qlinear.py:380-424 -- over the whole sweep
+    on cuda:0, one warm-up pass then `reps` timed passes (CUDA events).  Its comfy_kitchen kernels are absent."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    pts = sweep_points(ms)
+    ws = {(k, n): reference_weight(types, k, n, k + n, dev) for (k, n) in SWEEP}
+    xs = {(k, m): reference_activation(m, k, 1000 + k + m, dev) for (k, _, m) in pts}
+
+    def one():
+        for (k, n, m) in pts:
+            ql.linear(xs[(k, m)], ws[(k, n)], None, backend="torch", quant_mode="ck")
+
+    one()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        one()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return ops_of(pts) * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12
+
+
 def run_reference(args, rank):
+    """The reference arm: the reference's own CPU qlinear (oracle/_ref) on the host cores, each step a bounded sample of
+    the sweep -- the three projections at M = --ref-rows tokens (2048, a point of the sweep) -- timed as executed.  The
+    reference's portable CUDA path is timed over the full sweep beside it.  Without oracle/_ref the numpy port of the
+    reference CPU path (oracle/qlinear_oracle.py) stands in, labelled kind "port"."""
     if rank != 0:
         return
     if args.workload != "sweep":
         run_reference_dit(args)
         return
+    import torch
+
     cores = os.cpu_count() or 1
-    ms = args.ms
+    torch.set_num_threads(cores)
     rows = args.ref_rows
-    vals = []
+    staged = load_reference()
+    sample = [(k, n, rows) for (k, n) in SWEEP]
+    if staged is not None:
+        ql, types = staged
+        ws = {(k, n): reference_weight(types, k, n, k + n, "cpu") for (k, n) in SWEEP}
+        xs = {k: reference_activation(rows, k, 1000 + k + rows, "cpu") for (k, _) in SWEEP}
+
+        def step():
+            for (k, n, m) in sample:
+                ql.linear(xs[k], ws[(k, n)], None, backend="torch", quant_mode="ck")
+        kind, what = "reference", "h3turbo.h3.qlinear.linear(x, w, backend='torch', quant_mode='ck') on CPU (the reference's own code)"
+    else:
+        sys.path.insert(0, str(ROOT))
+        from oracle import qlinear_oracle as orc
+
+        wn = {(k, n): orc.synth_weight_int4_g128(n, k, seed=k + n) for (k, n) in SWEEP}
+        xn = {k: orc.synth_activation(rows, k, seed=1000 + k + rows, outlier_frac=0.005) for (k, _) in SWEEP}
+
+        def step():
+            for (k, n, m) in sample:
+                q, s_rel, s_ch, cb = wn[(k, n)]
+                orc.linear(xn[k], "bf16", q, s_rel, "fp16", s_ch, cb, 128)
+        kind, what = "port", "numpy restatement of the reference CPU qlinear (oracle/qlinear_oracle.py)"
+    times = []
     for i in range(args.warmup + args.steps):
-        v, detail = cpu_reference_rate(ms, rows)
+        t0 = time.perf_counter()
+        step()
         if i >= args.warmup:
-            vals.append(v)
-    value = statistics.median(vals)
-    line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ops_of(sweep_points(ms)) / (value * 1e12) * 1e3, "higher_is_better": True, "scaling": "weak",
+            times.append(time.perf_counter() - t0)
+    t_step = statistics.median(times)
+    value = ops_of(sample) / t_step / 1e12
+    # the full sweep at the same per-token rate (every call decodes its weight, so small M runs slower and large M
+    # faster than this): context only, not measured
+    extrap = ops_of(sweep_points(args.ms)) / (t_step * sum(m for m in args.ms) / rows / 1.0) / 1e12
+    cuda = None
+    if staged is not None and not args.no_ref_cuda:
+        try:
+            if torch.cuda.is_available():
+                cuda = {"value": reference_cuda_rate(ql, types, args.ms), "unit": "TOPS", "points": "the full sweep",
+                        "what": "the reference's portable CUDA path, qlinear.linear(backend='torch') on cuda:0: cuBLAS "
+                                "rotation, ck quantiser, per-call grid decode, torch._int_mm (its comfy_kitchen kernels "
+                                "are not available)"}
+        except Exception as e:  # a library limitation of the reference must not cost the CPU measurement
+            cuda = {"value": None, "error": repr(e)[:300]}
+    line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
-            "config": config_dict(ms, args.gpus),
-            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": "port",
-                             "sample": f"{rows} tokens and {CPU_WEIGHT_ROWS} output channels per projection (decode, quantise, "
-                                       f"int8 GEMM, epilogue), scaled per output channel and extrapolated per token to the "
-                                       f"sweep (numpy oracle of the reference CPU path, {cores} threads)",
-                             "detail": detail},
+            "config": config_dict(args.ms, args.gpus),
+            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": kind,
+                             "sample": f"each step: the three sweep projections at M = {rows} tokens (points of the sweep), "
+                                       f"timed as executed with {cores} threads: {what}",
+                             "extrapolated_full_sweep_tops": extrap,
+                             "extrapolation": "per token from the sample (the reference decodes the weight on every "
+                                              "call: context only, not measured)"},
+            "reference_cuda_path": cuda,
             "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_dit(args):
+    """Reference arm of the DiT workloads: the block's four W4A8 linears through the reference's own CPU qlinear on a
+    bounded token sample (attention, norms and RoPE excluded: an upper bound on the reference's CPU block rate)."""
+    import torch
+
+    tokens, nb, _, metric, cfg = dit_shape(args.workload)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    staged = load_reference()
+    rows = args.ref_rows
+    if staged is None:
+        v, detail = cpu_block_rate(tokens, nb, rows)
+        kind, t_ms, sample = "port", tokens / v * 1e3, f"numpy port, {rows}-token sample, extrapolated"
+    else:
+        ql, types = staged
+        ws = [reference_weight(types, k, n, 7 + k + n, "cpu") for (k, n) in BLOCK_LINEARS]
+        xs = [reference_activation(rows, k * (2 if j == 3 else 1), 11 + k, "cpu") for j, (k, _) in enumerate(BLOCK_LINEARS)]
+        times = []
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            for j, w in enumerate(ws):
+                ql.linear(xs[j], w, None, backend="torch", quant_mode="ck", input_act="swiglu" if j == 3 else None)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+        t_ms = statistics.median(times) * 1e3
+        v = rows / (t_ms * 1e-3) / nb
+        kind, sample = "reference", (f"the block's four W4A8 linears (qkv, out, fc1, fc2 with SwiGLU input) through the "
+                                     f"reference's own CPU qlinear on {rows} tokens, timed as executed ({cores} threads); "
+                                     f"tokens/s of {nb} block(s); attention, norms and RoPE excluded (an upper bound)")
+    cfg = dict(cfg, parallelism=f"{args.gpus} GPU(s) requested; the CPU arm runs on rank 0's host cores")
+    line = {"metric": metric, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference", "config": cfg,
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -285,90 +439,6 @@ def dit_shape(workload):
                        f"FFN {FFN} SwiGLU, W4A8 linears, bf16 attention/norms, AdaLN modulation precomputed",
            "model": "H3 DiT block, W4A8 int4 group-128 fp16 scales", "tokens": t, "blocks": nb}
     return t, nb, vid, f"DiT block tokens/s ({name})", cfg
-
-
-def run_reference_dit(args):
-    tokens, nb, _, metric, cfg = dit_shape(args.workload)
-    cores = os.cpu_count() or 1
-    vals = []
-    for i in range(args.warmup + args.steps):
-        v, detail = cpu_block_rate(tokens, nb, args.ref_rows)
-        if i >= args.warmup:
-            vals.append(v)
-    value = statistics.median(vals)
-    cfg = dict(cfg, parallelism=f"{args.gpus} GPU(s) requested; the CPU arm runs on rank 0's host cores")
-    line = {"metric": metric, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": tokens / value * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference", "config": cfg,
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": f"the four W4A8 linears only (attention, norms, RoPE excluded: an upper bound), "
-                                       f"{args.ref_rows} tokens and {CPU_WEIGHT_ROWS} output channels per projection, scaled per channel, per-token "
-                                       f"extrapolation to {tokens} tokens x {nb} blocks ({cores} threads)",
-                             "detail": detail},
-            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
-
-
-# ------------------------------------------------------------------------------------------------ torch GPU path
-def torch_path_linear(x, w, n_rows_budget=128 << 20):
-    """The reference's own portable CUDA path restated on library kernels (qlinear.py:_TorchRunner :380-405): decode
-    the int8 grid with the generic-scale formula (:193-199), then per token chunk (the :391 int32 budget) the tiled
-    bf16 x H rotation with fp32 output (:84-104), the "ck" quantiser (:278-292), cuBLASLt torch._int_mm (:236-247) and
-    the (acc * xs) * s_ch epilogue (:400-401).  A measurement baseline for the B200 kernels, never the product path."""
-    import torch
-
-    from minimax_h3_turbo_b200.h3.qlinear import hadamard_regular
-
-    n, k = w.q.shape[0], w.q.shape[1] * 2
-    q = w.q.view(torch.uint8).to(torch.int32)
-    code = torch.empty(n, k, dtype=torch.int32, device=x.device)
-    code[:, 0::2] = q & 0xF
-    code[:, 1::2] = q >> 4
-    vals = w.codebook.float()[code].view(n, -1, w.group_size) * w.s_rel.float().unsqueeze(-1)
-    w8 = vals.view(n, k).round_().clamp_(-127, 127).to(torch.int8)
-    del q, code, vals
-    ws = w.s_ch.float().reshape(1, -1)
-    h = hadamard_regular(w.convrot, x.device, x.dtype)
-    m = x.shape[0]
-    out = torch.empty(m, n, dtype=x.dtype, device=x.device)
-    step = max(32, n_rows_budget // (4 * n))
-    for a in range(0, m, step):
-        xc = x[a:a + step]
-        rows = xc.reshape(-1, w.convrot)
-        y32 = torch.empty(rows.shape[0], w.convrot, dtype=torch.float32, device=x.device)
-        for t in range(0, rows.shape[0], 4096):
-            torch.mm(rows[t:t + 4096], h, out=y32[t:t + 4096], out_dtype=torch.float32)
-        y32 = y32.view(xc.shape[0], k)
-        mn, mx = torch.aminmax(y32, dim=-1, keepdim=True)
-        xs = (torch.maximum(mx, -mn) / 127.0).clamp_(min=1e-30)
-        sc = xs.to(x.dtype)
-        sc = torch.where(sc == 0, torch.full_like(sc, torch.finfo(x.dtype).tiny), sc)
-        yq = y32.to(x.dtype).div_(sc).round_().clamp_(-128, 127).to(torch.int8)
-        rows_c = yq.shape[0]
-        if rows_c <= 16:  # cuBLASLt int8 wants M > 16 (the reference pads to 32, :241-245)
-            yq = torch.nn.functional.pad(yq, (0, 0, 0, 32 - rows_c))
-        acc = torch._int_mm(yq, w8.t())[:rows_c]
-        torch.mul(torch.mul(acc, xs), ws, out=out[a:a + step])
-    return out
-
-
-def torch_path_rate(points, weights, acts, dev, reps=1):
-    """TOPS of the torch GPU path over the sweep (1 warm-up pass, then `reps` timed passes, CUDA events)."""
-    import torch
-
-    def one():
-        for (k, n, m) in points:
-            torch_path_linear(acts[(k, m)], weights[(k, n)][0])
-
-    one()
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        one()
-    e1.record()
-    torch.cuda.synchronize(dev)
-    return ops_of(points) * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12
 
 
 # ------------------------------------------------------------------------------------------------ DiT workloads (GPU)
@@ -458,32 +528,70 @@ def dit_common_fields(pk, lin_ops, lin_ms, attn_flops, total_ms, steps):
                                   "attention_tflops_if_all_rest": attn_flops / (rest_ms * 1e-3) / 1e12 if rest_ms > 0 else None}}
 
 
-def run_dit(args, rank, world, local):
-    """Configs 3 and 5: DiT blocks on a video + audio sequence, token-sharded over the ranks (K/V all-gathered per
-    block, the final hidden states all-gathered at the sequence boundary)."""
+class PhaseProbe:
+    """CUDA events at the attention's phase boundaries (DiTBlock's probe): per block call, the exposed key/value
+    exchange time (kv_ready after qk_ready, or after local_done when the local attention overlaps the exchange) and
+    the attention time (the rest of qk_ready -> attn_done)."""
+
+    def __init__(self):
+        self.on, self.calls, self.cur = False, [], None
+
+    def __call__(self, tag):
+        import torch
+
+        if not self.on:
+            return
+        if tag == "qk_ready":
+            self.cur = {}
+            self.calls.append(self.cur)
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.cur[tag] = ev
+
+    def totals_ms(self):
+        exch = attn = 0.0
+        for c in self.calls:
+            if "kv_ready" not in c:
+                attn += c["qk_ready"].elapsed_time(c["attn_done"])
+                continue
+            start = c.get("local_done", c["qk_ready"])
+            exch += start.elapsed_time(c["kv_ready"])
+            attn += c["kv_ready"].elapsed_time(c["attn_done"])
+            if "local_done" in c:
+                attn += c["qk_ready"].elapsed_time(c["local_done"])
+        return exch, attn
+
+
+def dit_measure(workload, steps, warmup, rank, world, local, group, kv_exchange="overlap", kv_groups=1, e2e=True,
+                check_rows=0):
+    """Configs 3 and 5 on the kernels: DiT blocks on a video + audio sequence, token-sharded over `world` ranks (keys
+    and values exchanged per block, the final hidden states all-gathered at the sequence boundary).  Times `steps`
+    forwards (after `warmup`) with CUDA events, max over ranks; per phase: the W4A8 linears, the exposed key/value
+    exchange, attention.  check_rows > 0 (several ranks): rank 0 recomputes the whole sequence alone and compares that
+    many rows, spread over every shard, of the gathered output.  Returns the record (on every rank)."""
     import torch
     import torch.distributed as dist
-    from datetime import timedelta
 
     load_package()
     from minimax_h3_turbo_b200.h3 import block as blk
 
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    frames, hh, ww, audio, nb = SEQS[args.workload]
-    tokens, _, _, metric, cfg = dit_shape(args.workload)
+    frames, hh, ww, audio, nb = SEQS[workload]
+    tokens, _, _, metric, cfg = dit_shape(workload)
     a, b = blk.shard_rows(tokens, world, rank)
-    spec = blk.ShardSpec(a, b, tokens, group=dist.group.WORLD if world > 1 else None, world=world, rank=rank)
+    spec = blk.ShardSpec(a, b, tokens, group=group if world > 1 else None, world=world, rank=rank)
     cos, sin, segs = dit_sequence(frames, hh, ww, audio, a, b, dev)
     weights = [synthetic_block(100 + i, dev) for i in range(nb)]  # the same seeds on every rank: replicated weights
     mods = [synthetic_modulation(200 + i, dev) for i in range(nb)]
     gx = torch.Generator(device=dev).manual_seed(7)
-    x0 = torch.randn(tokens, HID, generator=gx, device=dev).to(torch.bfloat16)[a:b].contiguous()
+    x_all = torch.randn(tokens, HID, generator=gx, device=dev).to(torch.bfloat16)
+    x0 = x_all[a:b].contiguous()
+    if not check_rows or world == 1 or rank != 0:
+        del x_all
     x = torch.empty_like(x0)
-    lin = TimedLinear()
-    block = blk.DiTBlock(HEADS, HEAD_DIM, linear=lin, kv_exchange=args.kv_exchange, fuse_norm=True, kv_groups=args.kv_groups)
+    lin, probe = TimedLinear(), PhaseProbe()
+    block = blk.DiTBlock(HEADS, HEAD_DIM, linear=lin, kv_exchange=kv_exchange, fuse_norm=True, kv_groups=kv_groups,
+                         probe=probe)
     stream = torch.cuda.current_stream(dev)
 
     def forward(xin):
@@ -495,10 +603,16 @@ def run_dit(args, rank, world, local):
 
     def barrier():
         if world > 1:
-            dist.barrier()
+            dist.barrier(group=group)
         torch.cuda.synchronize(dev)
 
-    for _ in range(args.warmup):
+    def max_over_ranks(v):
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        return float(t.item())
+
+    for _ in range(warmup):
         forward(x0)
     barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -506,28 +620,55 @@ def run_dit(args, rank, world, local):
     clocks.start()
     barrier()
     clocks.begin()
-    lin.on = True
+    lin.on = probe.on = True
     t0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         out = forward(x0)
     t1.record(stream)
     barrier()
     clocks.end()
-    lin.on = False
+    lin.on = probe.on = False
     clk = clocks.stop()
-    t_local = torch.tensor([t0.elapsed_time(t1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
-    t_ms = float(t_local.item())
+    t_ms = max_over_ranks(t0.elapsed_time(t1))
+    lin_ms = max_over_ranks(lin.ms()) / steps
+    exch_ms, attn_ms = probe.totals_ms()
+    exch_ms, attn_ms = max_over_ranks(exch_ms) / steps, max_over_ranks(attn_ms) / steps
     finite = bool(torch.isfinite(out.float()).all().item()) and tuple(out.shape) == (tokens, HID)
-
-    # e2e: this rank's input rows from pinned host memory, the gathered output back to pinned host memory (rank 0)
-    e2e = None
-    if not args.no_e2e:
-        hin = torch.empty(b - a, HID, dtype=torch.bfloat16, pin_memory=True)
+    rows = b - a
+    kv_bytes = 2 * (tokens - rows) * HEADS * HEAD_DIM * 2  # keys + values this rank receives per block
+    rec = {"workload": cfg["workload"], "tokens": tokens, "blocks": nb, "n_gpus": world,
+           "tokens_per_s": tokens * steps / (t_ms * 1e-3), "ms_per_forward": t_ms / steps, "steps": steps,
+           "warmup": warmup, "qlinear_ms_per_forward": lin_ms, "attention_ms_per_forward": attn_ms,
+           "kv_exchange": kv_exchange if world > 1 else "none (one GPU)",
+           "kv_exchange_exposed_ms_per_forward": exch_ms,
+           "kv_bytes_in_per_rank_per_block": kv_bytes,
+           "kv_exchange_gbs_per_rank": (kv_bytes * nb / (exch_ms * 1e-3) / 1e9) if exch_ms > 0 else None,
+           "rest_ms_per_forward": t_ms / steps - lin_ms - attn_ms - exch_ms,
+           "rows_per_rank": [e - s for s, e in (blk.shard_rows(tokens, world, r) for r in range(world))],
+           "backend": dist.get_backend(group) if world > 1 else None, "nccl_ranks": world if world > 1 else 0,
+           "output_finite": finite, "clocks": clk,
+           "linear_tops_per_rank": nb * rows * BLOCK_OPS_PER_TOKEN / (lin_ms * 1e-3) / 1e12 if lin_ms > 0 else None,
+           "attention_tflops_per_rank": nb * 4.0 * rows * tokens * HEADS * HEAD_DIM / (attn_ms * 1e-3) / 1e12
+           if attn_ms > 0 else None}
+    if check_rows and world > 1:
+        idx = torch.linspace(0, tokens - 1, check_rows, device=dev).round().long()
+        got = out[idx].float()
+        if rank == 0:  # the same sequence on this GPU alone
+            ref_block = blk.DiTBlock(HEADS, HEAD_DIM, fuse_norm=True)
+            cos1, sin1, segs1 = dit_sequence(frames, hh, ww, audio, 0, tokens, dev)
+            y = x_all.clone()
+            for i in range(nb):
+                y = ref_block(y, weights[i], mods[i], segs1, cos1, sin1)
+            want = y[idx].float()
+            rec["check"] = {"rows": check_rows, "max_rel": float((got - want).abs().max() / want.abs().max()),
+                            "vs": "the same rows of the whole sequence recomputed on rank 0 alone (one GPU, no exchange)"}
+            del y, x_all
+        barrier()
+    if e2e:
+        hin = torch.empty(rows, HID, dtype=torch.bfloat16, pin_memory=True)
         hin.copy_(x0)
         hout = torch.empty(tokens, HID, dtype=torch.bfloat16, pin_memory=True)
-        e_steps = max(1, min(args.steps, 2))
+        e_steps = max(1, min(steps, 2))
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -537,43 +678,60 @@ def run_dit(args, rank, world, local):
                 hout.copy_(y, non_blocking=True)
         e1.record(stream)
         barrier()
-        te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": tokens * e_steps / (float(te.item()) * 1e-3), "unit": "tokens/s",
-               "h2d_bytes_per_step": tokens * HID * 2, "d2h_bytes_per_step": tokens * HID * 2, "steps": e_steps,
-               "path": "DiTBlock over qlinear.linear; each rank copies its input rows in from pinned host memory, rank 0 "
-                       "copies the gathered [tokens, 5120] output out"}
+        te = max_over_ranks(e0.elapsed_time(e1))
+        rec["e2e"] = {"value": tokens * e_steps / (te * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": tokens * HID * 2,
+                      "d2h_bytes_per_step": tokens * HID * 2, "steps": e_steps,
+                      "path": "DiTBlock over qlinear.linear; each rank copies its input rows in from pinned host memory, "
+                              "rank 0 copies the gathered [tokens, 5120] output out"}
+    rec["_lin_calls"] = lin.calls
+    rec["_metric"], rec["_cfg"] = metric, cfg
+    del weights, out, x, x0
+    torch.cuda.empty_cache()
+    return rec
 
+
+def run_dit(args, rank, world, local):
+    """Configs 3 and 5 as their own bench line (`--workload block|longseq`)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    group = dist.group.WORLD if world > 1 else None
+    rec = dit_measure(args.workload, args.steps, args.warmup, rank, world, local, group, args.kv_exchange,
+                      args.kv_groups, e2e=not args.no_e2e, check_rows=256 if world > 1 else 0)
+    tokens, nb = rec["tokens"], rec["blocks"]
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cores = os.cpu_count() or 1
         v, detail = cpu_block_rate(tokens, nb, args.cpu_rows)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"the four W4A8 linears only (attention, norms, RoPE excluded: an upper bound), {args.cpu_rows} "
-                         f"tokens and {CPU_WEIGHT_ROWS} output channels per projection, scaled per channel, per-token extrapolation ({cores} threads)",
-               "detail": detail}
-
-    rows = b - a
+                         f"tokens and {CPU_WEIGHT_ROWS} output channels per projection, scaled per channel, per-token "
+                         f"extrapolation ({cores} threads)", "detail": detail}
+    rows = tokens // world
     lin_ops = nb * rows * BLOCK_OPS_PER_TOKEN
     attn_flops = nb * 4.0 * rows * tokens * HEADS * HEAD_DIM
-    fields = dit_common_fields(peaks(), lin_ops, lin.ms(), attn_flops, t_ms if world == 1 else t0.elapsed_time(t1), args.steps)
+    fields = dit_common_fields(peaks(), lin_ops, rec["qlinear_ms_per_forward"] * args.steps, attn_flops,
+                               rec["ms_per_forward"] * args.steps, args.steps)
     if rank == 0:
-        exch = "K/V shards passed round a ring of the ranks, overlapped with attention" if args.kv_exchange == "ring" \
-            else (f"K/V all-gather per block in {args.kv_groups} head groups, each group's attention overlapping the later "
-                  "groups' gathers" if args.kv_groups > 1 else "K/V all-gather per block")
-        cfg = dict(cfg, parallelism=f"token-shard x{world} (contiguous rows, {exch}, output all-gather)",
-                   rows_per_rank=[e - s for s, e in (blk.shard_rows(tokens, world, r) for r in range(world))],
+        cfg = dict(rec["_cfg"], parallelism=f"token-shard x{world} (contiguous rows, K/V exchange: {rec['kv_exchange']}, "
+                                            f"output all-gather)", rows_per_rank=rec["rows_per_rank"],
                    l2="inputs larger than L2 (each block streams ~0.6 GB of weights+activations per rank)")
-        line = {"metric": metric, "value": tokens * args.steps / (t_ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": cfg, **fields,
-                "linear_tops_whole_job": world * lin_ops * args.steps / (t_ms * 1e-3) / 1e12,
-                "output_finite": finite, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+        detail = {k: v for k, v in rec.items() if not k.startswith("_") and k not in ("e2e", "clocks")}
+        line = {"metric": rec["_metric"], "value": rec["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": rec["ms_per_forward"],
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+                "config": cfg, **fields, "phases": detail, "cpu_baseline": cpu, "e2e": rec.get("e2e"),
+                "clocks": rec["clocks"],
                 # per block: 4 W4A8 linears (rotate+quantise -- with the RMSNorm+modulation for qkv and fc1 --, decode,
-                # GEMM each), 1 q/k norm+RoPE, 2 gated residuals, and with the ring exchange one attention merge per key
-                # shard
-                "gpu_launches": 3 * lin.calls + (3 + (world if world > 1 and args.kv_exchange == "ring" else 0)) * nb * args.steps}
+                # GEMM each), 1 q/k norm+RoPE, 2 gated residuals, with the overlapped or ring exchange the merges
+                "gpu_launches": 3 * rec["_lin_calls"] + 3 * nb * args.steps +
+                (2 * nb * args.steps if world > 1 and args.kv_exchange == "overlap" else 0) +
+                (world * nb * args.steps if world > 1 and args.kv_exchange == "ring" else 0)}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -749,16 +907,19 @@ def main():
     ap.add_argument("--ms", default=",".join(map(str, MS)))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--no-torch-path", action="store_true", help="skip timing the torch restatement of the reference's CUDA path")
     ap.add_argument("--cpu-rows", type=int, default=256)
-    ap.add_argument("--ref-rows", type=int, default=256)
+    ap.add_argument("--ref-rows", type=int, default=2048, help="reference arm: tokens per projection in each step's sample")
+    ap.add_argument("--no-ref-cuda", action="store_true", help="reference arm: skip timing the reference's CUDA path")
     ap.add_argument("--detail", default="", help="write per-point timings to this JSON file")
     ap.add_argument("--workload", default="sweep", choices=WORKLOADS,
                     help="sweep: config 2 (default); block: config 3; stream: config 4; longseq: config 5")
     ap.add_argument("--store-dir", default="", help="stream workload: directory for the temporary ~7.9 GB h3t store")
     ap.add_argument("--kv-groups", type=int, default=1, help="block/longseq over several GPUs: head groups of the K/V all-gather")
-    ap.add_argument("--kv-exchange", default="gather", choices=["ring", "gather"],
-                    help="block/longseq on several GPUs: key/value shards passed round a ring (overlapped) or all-gathered")
+    ap.add_argument("--kv-exchange", default="overlap", choices=["overlap", "gather", "ring"],
+                    help="DiT blocks on several GPUs: keys/values exchanged point-to-point behind the local attention "
+                         "(overlap), all-gathered first (gather), or passed round a ring")
+    ap.add_argument("--dit-steps", type=int, default=5, help="sweep line: timed forwards of the config-5 record (config 3: twice as many)")
+    ap.add_argument("--no-dit", action="store_true", help="sweep line: skip the config-5 (and, on one GPU, config-3) records")
     args = ap.parse_args()
     args.ms = [int(v) for v in args.ms.split(",") if v]
     rank, world, local = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
@@ -775,6 +936,32 @@ def main():
         run_stream(args, rank, world, local)
         return
     run_sweep(args, rank, world, local)
+
+
+def measure_int8_peak(dev, n=8192, reps=10):
+    """Dense int8 tensor-core throughput of the library GEMM on this GPU: torch._int_mm (cuBLASLt) on n^3, best of
+    `reps` launches timed with CUDA events."""
+    import torch
+
+    try:
+        g = torch.Generator(device=dev).manual_seed(0)
+        a = torch.randint(-128, 128, (n, n), generator=g, device=dev, dtype=torch.int32).to(torch.int8)
+        b = torch.randint(-128, 128, (n, n), generator=g, device=dev, dtype=torch.int32).to(torch.int8)
+        bt = b.t()  # column-major operand, the layout cuBLASLt's int8 kernels take
+        for _ in range(3):
+            torch._int_mm(a, bt)
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, bt)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            best = min(best, e0.elapsed_time(e1))
+        del a, b, bt
+        return {"tops": 2.0 * n ** 3 / (best * 1e-3) / 1e12, "how": f"torch._int_mm (cuBLASLt) {n}^3 int8 -> int32, best of {reps}"}
+    except Exception as e:  # a library limitation must not cost the main measurement
+        return {"tops": None, "error": repr(e)[:200]}
 
 
 def run_sweep(args, rank, world, local):
@@ -893,10 +1080,10 @@ def run_sweep(args, rank, world, local):
     gemm_tops = ops_step / (tot["gemm"] * 1e-3) / 1e12
     rotq_bytes = sum(3.0 * m * k + 4.0 * m for (k, _, m) in points)
     rotq_gbs = rotq_bytes / (tot["rotq"] * 1e-3) / 1e9
-    # DRAM bytes (read + write) per algorithmic op of the GEMM, from the ncu capture summarised in
-    # profiles/gemm_i8_kernel_sweep_m16384.md (K = N = 5120, M = 16384: 349.9 MB for 859.0 GOP), scaled to the average
-    # GEMM launch of this sweep
-    traffic = GEMM_DRAM_BYTES_PER_OP * ops_step / len(points)
+    # DRAM bytes (read + write) of the GEMM launch of each point, measured with ncu on a B200 (dram__bytes_read.sum +
+    # dram__bytes_write.sum of that kernel, this sweep's command): the average launch of the sweep, or None when a
+    # point of this run was not measured
+    traffic = (sum(GEMM_DRAM_BYTES[p] for p in points) / len(points)) if all(p in GEMM_DRAM_BYTES for p in points) else None
 
     # ---- e2e through the public API with pinned host buffers (copies inside the timed region)
     e2e = None
@@ -959,17 +1146,6 @@ def run_sweep(args, rank, world, local):
                "path": "qlinear.linear (public API) per point; pinned host input/output; uploads, compute and downloads "
                        "pipelined on three streams (two device input slots)"}
 
-    # ---- the reference's own CUDA algorithm on library kernels (cuBLAS rotation, cuBLASLt int8 GEMM), same GPU
-    torch_path = None
-    if world == 1 and not args.no_torch_path:
-        try:
-            torch_path = {"value": torch_path_rate(points, weights, acts, dev), "unit": "TOPS",
-                          "what": "the reference's portable CUDA path (decode, tiled cuBLAS rotation, ck quantiser, "
-                                  "torch._int_mm, epilogue) restated on torch ops, same sweep and GPU"}
-        except Exception as e:  # a library limitation must not cost the main measurement
-            torch_path = {"value": None, "error": repr(e)[:200]}
-            torch.cuda.synchronize(dev)
-
     # ---- CPU baseline (rank 0, single GPU only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -980,6 +1156,22 @@ def run_sweep(args, rank, world, local):
                          f"int8 GEMM, epilogue), scaled per output channel and extrapolated per token to the sweep "
                          f"(numpy oracle of the reference CPU path, {cores} threads)",
                "detail": detail}
+
+    # ---- a measured int8 denominator beside 2 x bf16: cuBLASLt's int8 GEMM (torch._int_mm) at 8192^3, best of 10
+    int8_lib = measure_int8_peak(dev)
+
+    # ---- the DiT records: config 5 token-sharded over the N ranks (every N), config 3 on one GPU
+    del weights, grids, acts, outs, codes, xs
+    torch.cuda.empty_cache()
+    sharded = block3 = None
+    if not args.no_dit:
+        group = dist.group.WORLD if world > 1 else None
+        rec = dit_measure("longseq", args.dit_steps, 3, rank, world, local, group, args.kv_exchange, args.kv_groups,
+                          e2e=False, check_rows=256 if world > 1 else 0)
+        sharded = {k: v for k, v in rec.items() if not k.startswith("_")}
+        if world == 1:
+            rec3 = dit_measure("block", 2 * args.dit_steps, 3, rank, world, local, None, e2e=False)
+            block3 = {k: v for k, v in rec3.items() if not k.startswith("_")}
 
     if args.detail and rank == 0:
         Path(args.detail).parent.mkdir(parents=True, exist_ok=True)
@@ -993,11 +1185,14 @@ def run_sweep(args, rank, world, local):
                                                            "the int4 decode for small M)", "achieved": gemm_tops, "peak": int8_peak,
                              "unit": "TOPS", "frac": gemm_tops / int8_peak, "traffic": traffic,
                              "peak_note": f"int8 dense = 2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s burst)",
-                             "frac_of_sustained": gemm_tops / (2.0 * pk["bf16_sustained"]) if pk.get("bf16_sustained") else None},
+                             "frac_of_sustained": gemm_tops / (2.0 * pk["bf16_sustained"]) if pk.get("bf16_sustained") else None,
+                             "int8_library_peak": int8_lib,
+                             "frac_of_int8_library": gemm_tops / int8_lib["tops"] if int8_lib.get("tops") else None},
                 "rotq_roofline": {"bound": "hbm", "kernel": "rotq_kernel", "achieved": rotq_gbs, "peak": pk["hbm_gbs"],
                                   "unit": "GB/s", "frac": rotq_gbs / pk["hbm_gbs"]},
-                "kernel_ms_per_step": tot, "cpu_baseline": cpu, "torch_gpu_path": torch_path, "e2e": e2e, "clocks": clk,
-                "gpu_launches": sum(2 if fused[p] else 3 for p in points) * args.steps}
+                "kernel_ms_per_step": tot, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "gpu_launches": sum(2 if fused[p] else 3 for p in points) * args.steps,
+                "sharded_block": sharded, "block": block3}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

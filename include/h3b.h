@@ -120,10 +120,12 @@ int h3b_gate_residual(void* x, int x_dtype, int64_t ldx, const void* other, int6
  * the token-sharded DiT block, whose single-GPU form is one attention call, model.py:196-228).  For every head h and
  * query q: L' = log(exp(L) + exp(l)), A = A exp(L - L') + fp32(o) exp(l - L'), L = L'.
  *   acc    fp32 [heads, queries, head_dim] running output;  acc_lse fp32 [heads, queries] running log-sum-exp
- *   o      bf16 attention output over the next key set, element (h, q, d) at o + h*o_head_stride + q*o_query_stride + d
+ *   o      attention output over the next key set, element (h, q, d) at o + h*o_head_stride + q*o_query_stride + d;
+ *          o_dtype must be H3B_BF16 (anything else is refused with H3B_ERR_ARG)
  *   lse    fp32 [heads, queries] its log-sum-exp (natural log);  first != 0: (acc, acc_lse) = (o, lse)
+ *          a query with no keys on either side (both log-sum-exps -inf) gets a zero output
  *   out    optional bf16 [queries, heads * head_dim] (row stride ldo): the merged result, written instead of acc */
-int h3b_attn_merge(float* acc, float* acc_lse, const void* o, int64_t o_head_stride, int64_t o_query_stride,
+int h3b_attn_merge(float* acc, float* acc_lse, const void* o, int64_t o_head_stride, int64_t o_query_stride, int o_dtype,
                    const float* lse, int64_t heads, int64_t queries, int head_dim, int first, void* out, int64_t ldo,
                    void* stream);
 
@@ -183,8 +185,9 @@ int h3b_w4a8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld
  * not call cudaMalloc (it can synchronise the whole device).  The decoded weight rows live in one file-scope device
  * array of H3B_NOALLOC_SCRATCH_BYTES that every GPU using the library holds until the process exits; the weight is
  * decoded and multiplied in slabs of rows that fit in it, so any N works, and K may be at most
- * H3B_NOALLOC_SCRATCH_BYTES / 32 (larger K is rejected with H3B_ERR_ARG).  The first call on a device looks up the
- * array's device address (once per device); make that first call before any stream capture.  All calls share the one
+ * H3B_NOALLOC_SCRATCH_BYTES / 32 (larger K is rejected with H3B_ERR_ARG).  Every call looks up the array's device
+ * address in the current device's context (cudaGetSymbolAddress; the first call on a device loads the module there, so
+ * make that first call before any stream capture).  All calls share the one
  * array: calls that may overlap on the GPU (different streams, or different host threads) race on it and must be
  * serialised by the caller.  Nothing in it needs to start at zero (each slab is fully rewritten before it is read). */
 #define H3B_NOALLOC_SCRATCH_BYTES (16u << 20)

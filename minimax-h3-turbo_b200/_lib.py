@@ -45,7 +45,7 @@ _SIGNATURES = {
                           _i64, _int, _c_void_p, _int, _c_void_p, _c_void_p, _i64, _c_void_p], _int),
     "h3b_gate_residual": ([_c_void_p, _int, _i64, _c_void_p, _i64, _i64, _int, _c_void_p, _i64, _i64, _int, _c_void_p, _int,
                            _c_void_p, _c_void_p], _int),
-    "h3b_attn_merge": ([_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _int, _int, _c_void_p, _i64,
+    "h3b_attn_merge": ([_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _int, _c_void_p, _i64, _i64, _int, _int, _c_void_p, _i64,
                         _c_void_p], _int),
     "h3b_w4a8_gemm_decodes_in_kernel": ([_i64, _i64, _i64, _c_void_p, _i64, _int, _int], _int),
     "h3b_decode_grid": ([_c_void_p, _i64, _i64, _i64, _c_void_p, _int, _i64, _c_void_p, _int, _c_void_p, _i64, _c_void_p], _int),

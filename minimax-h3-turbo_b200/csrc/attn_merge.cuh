@@ -30,14 +30,19 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(float* __restrict__ acc
     } else {
       const float L = acc_lse[row];
       const float m = fmaxf(L, l);
-      // log(exp(L) + exp(l)) = m + log(exp(L - m) + exp(l - m)), both exponents <= 0
-      const float ea = expf(L - m), eb = expf(l - m);
-      const float sum = ea + eb;
-      const float wa = ea / sum, wb = eb / sum;
+      if (m == -INFINITY) {  // neither key set had a key for this query (empty shards): nothing to weigh, output 0
 #pragma unroll
-      for (int i = 0; i < VPL; ++i)
-        res[i] = fmaf(arow[lane + 32 * i], wa, __bfloat162float(orow[lane + 32 * i]) * wb);
-      if (lane == 0) acc_lse[row] = m + logf(sum);
+        for (int i = 0; i < VPL; ++i) res[i] = 0.f;
+      } else {
+        // log(exp(L) + exp(l)) = m + log(exp(L - m) + exp(l - m)), both exponents <= 0; an empty side has weight 0
+        const float ea = expf(L - m), eb = expf(l - m);
+        const float sum = ea + eb;
+        const float wa = ea / sum, wb = eb / sum;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i)
+          res[i] = fmaf(wa == 0.f ? 0.f : arow[lane + 32 * i], wa, wb == 0.f ? 0.f : __bfloat162float(orow[lane + 32 * i]) * wb);
+        if (lane == 0) acc_lse[row] = m + logf(sum);
+      }
     }
     if (out) {
       __nv_bfloat16* dst = out + q * ldo + h * D;

@@ -85,26 +85,17 @@ static int check_weight_args(const void* q4, int64_t N, int64_t K, int64_t ldq4,
 // h3b_w4a8_gemm_noalloc: the same decode + GEMM + epilogue as h3b_w4a8_gemm, for callers that cannot allocate device
 // memory (see include/h3b.h).  Its scratch -- the decoded int8 weight rows -- is this file-scope device array.  In host
 // code `g_noalloc_grid` names a host-side stand-in, not device memory, so its device address is looked up with
-// cudaGetSymbolAddress once per device (with that device current) and only that address is handed to the kernels.
+// cudaGetSymbolAddress (with the caller's device current) and only that address is handed to the kernels.
 static __device__ __align__(256) int8_t g_noalloc_grid[H3B_NOALLOC_SCRATCH_BYTES];
 
 namespace h3b {
-static std::mutex g_noalloc_mu;
-static void* g_noalloc_addr[64] = {};
-
+// The array's device address in the current device's current context.  Looked up on every call (cheap once the module
+// is loaded) rather than cached, so a device reset or a different context on the same ordinal never sees a stale address.
 static int noalloc_scratch(void** addr) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(H3B_ERR_UNSUPPORTED, "device ordinal >= 64");
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_grid);
-    if (e != cudaSuccess || !p) return cuda_fail(e, "cudaGetSymbolAddress(allocation-free scratch)");
-    g_noalloc_addr[dev] = p;
-  }
-  *addr = g_noalloc_addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_grid);
+  if (e != cudaSuccess || !p) return cuda_fail(e, "cudaGetSymbolAddress(allocation-free scratch)");
+  *addr = p;
   return H3B_OK;
 }
 // The failure path of the bounded waits, exercised on purpose: one thread waits on an mbarrier that nothing arrives on;
@@ -260,9 +251,10 @@ int h3b_gate_residual(void* x, int x_dtype, int64_t ldx, const void* other, int6
                               static_cast<cudaStream_t>(stream));
 }
 
-int h3b_attn_merge(float* acc, float* acc_lse, const void* o, int64_t o_head_stride, int64_t o_query_stride,
+int h3b_attn_merge(float* acc, float* acc_lse, const void* o, int64_t o_head_stride, int64_t o_query_stride, int o_dtype,
                    const float* lse, int64_t heads, int64_t queries, int head_dim, int first, void* out, int64_t ldo,
                    void* stream) {
+  if (o_dtype != H3B_BF16) return fail(H3B_ERR_ARG, "attn_merge: the attention output (and the merged output) must be bf16");
   if (heads < 0 || queries < 0) return fail(H3B_ERR_ARG, "attn_merge: negative size");
   if (heads == 0 || queries == 0) return H3B_OK;
   if (!acc || !acc_lse || !o || !lse) return fail(H3B_ERR_ARG, "attn_merge: null pointer");

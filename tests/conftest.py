@@ -12,8 +12,9 @@ import numpy as np
 import pytest
 
 ROOT = Path(__file__).resolve().parent.parent
-if str(ROOT) not in sys.path:
-    sys.path.insert(0, str(ROOT))
+for _p in (ROOT, ROOT / "tests" / "helpers"):  # the repo root (oracle) and the test helpers (torch_ops, ...)
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
 os.environ.setdefault("OMP_NUM_THREADS", "4")
 
 

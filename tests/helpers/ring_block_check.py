@@ -1,6 +1,6 @@
 """Run by tests/test_block_gpu.py under torchrun (2 ranks, one GPU each): the token-sharded DiT block with the ring and
-the all-gather key/value exchanges (in head groups, and all at once) against the unsharded block on rank 0's GPU.
-Prints RING_OK / GATHER_OK / GATHER1_OK."""
+the all-gather key/value exchanges (in head groups, and all at once) and the overlapped point-to-point exchange
+against the unsharded block on rank 0's GPU.  Prints RING_OK / GATHER_OK / GATHER1_OK / OVERLAP_OK."""
 import os
 import sys
 from datetime import timedelta
@@ -41,7 +41,8 @@ def main():
         spec = blk.ShardSpec(a, b, S, dist.group.WORLD, world, rank)
         segs = [(max(s0, a) - a, min(s1, b) - a, r) for s0, s1, r in segs_full if min(s1, b) > max(s0, a)]
         # gather: K/V all-gathered in 4 head groups (one head each here); gather1: all heads at once
-        for mode, exchange, groups in (("ring", "ring", 1), ("gather", "gather", 4), ("gather1", "gather", 1)):
+        for mode, exchange, groups in (("ring", "ring", 1), ("gather", "gather", 4), ("gather1", "gather", 1),
+                                       ("overlap", "overlap", 1)):
             block = blk.DiTBlock(HEADS, HD, kv_exchange=exchange, kv_groups=groups)
             y = block(x[a:b].clone(), w, mod, segs, cos[a:b], sin[a:b], spec)
             full = blk.gather_rows(y, spec)

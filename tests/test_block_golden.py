@@ -1,9 +1,11 @@
 """The DiT block composition against the reference's own block (tests/golden/block_golden.npz), on CPU: our DiTBlock with
-the oracle as its linear runs the same torch ops the reference runs on CPU (F.rms_norm, modulation, the exact "torch"
-form of q/k norm + RoPE, SDPA, gating), so every intermediate and the output must match bit for bit."""
+the oracle as its linear and the reference's torch operators (tests/helpers/torch_ops.py: F.rms_norm, modulation, the
+exact "torch" form of q/k norm + RoPE, SDPA, gating) must match every intermediate and the output bit for bit -- the
+block's composition (order of the steps, what each one reads) is the reference's."""
 import numpy as np
 import torch
 
+import torch_ops as tops
 from minimax_h3_turbo_b200.h3 import block as blk
 from oracle import qlinear_oracle as orc
 
@@ -19,8 +21,8 @@ def oracle_linear(x, w, input_act=None):
 
 def test_block_equals_the_reference_block_on_cpu():
     w, mod, segs, (hid, heads, hd, ffn), (eps, qk_eps), t = bg.load()
-    block = blk.DiTBlock(heads, hd, eps, qk_eps, linear=oracle_linear)
-    h1 = blk.rms_modulate(t["x"], w.norm1, eps, mod.shift_a, mod.scale_a, segs)
+    block = blk.DiTBlock(heads, hd, eps, qk_eps, linear=oracle_linear, ops=tops.TorchOps())
+    h1 = tops.rms_modulate(t["x"], w.norm1, eps, mod.shift_a, mod.scale_a, segs)
     assert torch.equal(h1, t["h1"])
     qkv = oracle_linear(t["h1"], w.qkv)
     assert torch.equal(qkv, t["qkv"])

@@ -3,6 +3,7 @@ the int8 activation quantisation noise, ~1 % per linear), query chunking, and th
 import pytest
 import torch
 
+import torch_ops as tops
 from minimax_h3_turbo_b200.h3 import block as blk
 from minimax_h3_turbo_b200.h3 import qlinear as ql
 from minimax_h3_turbo_b200.h3.synth import synthetic_activation, synthetic_w4a8
@@ -38,7 +39,7 @@ def _dense_reference(w):
             t = torch.nn.functional.silu(g) * u
         return t @ wt.t()
 
-    return blk.DiTBlock(HEADS, HD, linear=lin), wd
+    return blk.DiTBlock(HEADS, HD, linear=lin, ops=tops.TorchOps()), wd
 
 
 def _rel(a, b):
@@ -50,7 +51,7 @@ def test_attention_and_mlp_branches_match_the_dequantized_fp32_block():
     per linear, outlier channels spread by the rotation) and bf16 intermediates."""
     x, w, mod, seg, cos, sin = make()
     ref_block, wd = _dense_reference(w)
-    h = blk.rms(x, w.norm1, 1e-5)
+    h = tops.rms(x, w.norm1, 1e-5)
     a = blk.DiTBlock(HEADS, HD).attention(h.clone(), w, cos, sin)
     a_ref = ref_block.attention(h.float(), wd, cos.float(), sin.float())
     m = blk.DiTBlock(HEADS, HD).mlp(h.clone(), w)
@@ -72,7 +73,7 @@ def test_block_matches_the_dequantized_fp32_block():
 def test_chunked_attention_matches():
     """Query rows are independent, so chunking changes only which attention kernel runs and its summation order."""
     x, w, mod, seg, cos, sin = make(1)
-    h = blk.rms(x, w.norm1, 1e-5)
+    h = tops.rms(x, w.norm1, 1e-5)
     a = blk.DiTBlock(HEADS, HD).attention(h.clone(), w, cos, sin)
     b = blk.DiTBlock(HEADS, HD, attn_chunk=64).attention(h.clone(), w, cos, sin)
     assert _rel(b, a) < 1e-2
@@ -125,7 +126,7 @@ def test_attention_over_key_chunks_merges_to_full_attention():
     acc = lse = None
     for a, b in ((0, 250), (250, 251), (251, 700)):
         o, l_ = blk.attention_lse(q, k[:, :, a:b], v[:, :, a:b])
-        acc, lse = blk.merge_attention(acc, lse, o, l_)
+        acc, lse = tops.merge_attention(acc, lse, o, l_)
     assert _rel(acc, want) < 1e-2, _rel(acc, want)
 
 
@@ -144,7 +145,8 @@ def test_ring_block_on_two_gpus_equals_one_gpu():
     env = dict(__import__("os").environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert "RING_OK" in r.stdout and "GATHER_OK" in r.stdout and "GATHER1_OK" in r.stdout, r.stdout[-3000:]
+    for tag in ("RING_OK", "GATHER_OK", "GATHER1_OK", "OVERLAP_OK"):
+        assert tag in r.stdout, r.stdout[-3000:]
 
 
 def test_fused_merge_kernel_equals_the_torch_merge():
@@ -161,11 +163,44 @@ def test_fused_merge_kernel_equals_the_torch_merge():
     ref = ref_lse = None
     for i, (k, v) in enumerate(kv):
         o, lse = blk.attention_lse(q, k, v)
-        ref, ref_lse = blk.merge_attention(ref, ref_lse, o, lse)
+        ref, ref_lse = tops.merge_attention(ref, ref_lse, o, lse)
         lse = lse.reshape(h, sq).contiguous()
         _lib.check(_lib.lib().h3b_attn_merge(acc.data_ptr(), lse_acc.data_ptr(), o.data_ptr(), o.stride(1), o.stride(2),
-                                             lse.data_ptr(), h, sq, d, int(i == 0),
+                                             _lib.BF16, lse.data_ptr(), h, sq, d, int(i == 0),
                                              out.data_ptr() if i == len(kv) - 1 else None, h * d,
                                              _lib.stream_ptr(DEV)), "merge")
     want = ref[0].transpose(0, 1).reshape(sq, h * d)
     assert _rel(out, want) < 5e-3, _rel(out, want)
+
+
+def test_merge_kernel_handles_empty_key_sets_and_refuses_other_dtypes():
+    """A key set with no keys has log-sum-exp -inf: merging it changes nothing, and two empty sides give zeros (not NaN)."""
+    from minimax_h3_turbo_b200 import _lib
+
+    h, sq, d = 2, 40, 128
+    g = torch.Generator(device=DEV).manual_seed(5)
+    o = torch.randn(1, h, sq, d, generator=g, device=DEV).to(torch.bfloat16)
+    lse = torch.randn(h, sq, generator=g, device=DEV)
+    empty_o = torch.zeros_like(o)
+    empty_lse = torch.full((h, sq), float("-inf"), device=DEV)
+    acc = torch.empty(h, sq, d, device=DEV)
+    acc_lse = torch.empty(h, sq, device=DEV)
+    out = torch.empty(sq, h * d, dtype=torch.bfloat16, device=DEV)
+    L = _lib.lib()
+
+    def merge(oo, ll, first, last):
+        _lib.check(L.h3b_attn_merge(acc.data_ptr(), acc_lse.data_ptr(), oo.data_ptr(), oo.stride(1), oo.stride(2), _lib.BF16,
+                                    ll.data_ptr(), h, sq, d, int(first), out.data_ptr() if last else None, h * d,
+                                    _lib.stream_ptr(DEV)), "merge")
+
+    merge(empty_o, empty_lse, True, False)
+    merge(o, lse, False, False)
+    merge(empty_o, empty_lse, False, True)
+    assert torch.equal(out, o[0].transpose(0, 1).reshape(sq, h * d))
+    assert torch.equal(acc_lse, lse)
+    merge(empty_o, empty_lse, True, False)
+    merge(empty_o, empty_lse, False, True)
+    assert torch.equal(out, torch.zeros_like(out))
+    rc = L.h3b_attn_merge(acc.data_ptr(), acc_lse.data_ptr(), o.data_ptr(), o.stride(1), o.stride(2), _lib.FP16,
+                          lse.data_ptr(), h, sq, d, 1, None, h * d, _lib.stream_ptr(DEV))
+    assert rc == _lib.ERR_ARG and b"bf16" in L.h3b_last_error()

@@ -2,6 +2,7 @@
 import pytest
 import torch
 
+import torch_ops as tops
 from minimax_h3_turbo_b200.h3 import block as blk
 
 pytestmark = pytest.mark.gpu
@@ -9,7 +10,7 @@ DEV = torch.device("cuda")
 
 
 def _ref(x, w, eps, sh, sc, segs):
-    return blk.scale_shift_(blk.rms(x, w, eps), sh, sc, segs)
+    return tops.scale_shift_(tops.rms(x, w, eps), sh, sc, segs)
 
 
 def _inputs(m, hid, dt, mdt, seed, int_valued=False):

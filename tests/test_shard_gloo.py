@@ -1,8 +1,9 @@
-"""Token sharding of the DiT block on CPU ranks (gloo, world size 2 and 3): the row split, the row all-gather and a
-sharded block -- K/V all-gathered (at once or in head groups), or passed round a ring with the attention merged by
-log-sum-exp; everything else
-token-wise -- equal the unsharded block.  The W4A8 linear is CUDA-only,
-so these ranks run the block with a dense fp32 linear; the GPU path swaps in the qlinear (tests/test_block_gpu.py)."""
+"""Token sharding of the DiT block on CPU ranks (gloo, world size 2 to 4): the row split, the row all-gather and a sharded
+block -- K/V exchanged point-to-point behind the local attention and merged by log-sum-exp ("overlap"), all-gathered
+(at once or in head groups), or passed round a ring; everything else token-wise -- equal the unsharded block.  The
+block's kernels are CUDA-only, so these ranks run it with a dense fp32 linear and the reference's torch operators
+(tests/helpers/torch_ops.py); the GPU path runs the kernels (tests/test_block_gpu.py).  Also: a rank that leaves
+between blocks, or never joins, makes the others raise within the process group's timeout instead of hanging."""
 import os
 import socket
 
@@ -12,6 +13,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import conftest  # noqa: F401  -- registers the package (also in the spawned ranks, which re-import this module)
+import torch_ops as tops
 from minimax_h3_turbo_b200.h3 import block as blk
 from minimax_h3_turbo_b200.h3.types import BlockWeights
 
@@ -62,7 +64,7 @@ def _worker(rank, world, port, q, exchange, groups):
         spec = blk.ShardSpec(a, b, S, dist.group.WORLD, world, rank)
         g = blk.gather_rows(torch.arange(a, b, dtype=torch.float32).view(-1, 1), spec)
         ok_gather = torch.equal(g.view(-1), torch.arange(S, dtype=torch.float32))
-        block = blk.DiTBlock(HEADS, HD, linear=dense, kv_exchange=exchange, kv_groups=groups)
+        block = blk.DiTBlock(HEADS, HD, linear=dense, kv_exchange=exchange, kv_groups=groups, ops=tops.TorchOps())
         y = block(x[a:b].clone(), w, mod, _segments(a, b), cos[a:b], sin[a:b], spec)
         full = blk.gather_rows(y, spec)
         q.put((rank, ok_gather, full))
@@ -70,12 +72,13 @@ def _worker(rank, world, port, q, exchange, groups):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,exchange,groups", [(2, "gather", 1), (3, "gather", 1), (2, "gather", 2), (3, "gather", 2),
+@pytest.mark.parametrize("world,exchange,groups", [(2, "overlap", 1), (3, "overlap", 1), (4, "overlap", 1),
+                                                  (2, "gather", 1), (3, "gather", 1), (2, "gather", 2), (3, "gather", 2),
                                                   (2, "ring", 1), (3, "ring", 1)])
 def test_sharded_block_equals_unsharded(world, exchange, groups):
     """groups = 2: the K/V all-gather in two head groups, both started before either group's attention."""
     x, w, mod, cos, sin = make_case()
-    ref = blk.DiTBlock(HEADS, HD, linear=dense)(x.clone(), w, mod, _segments(0, S), cos, sin)
+    ref = blk.DiTBlock(HEADS, HD, linear=dense, ops=tops.TorchOps())(x.clone(), w, mod, _segments(0, S), cos, sin)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
@@ -91,6 +94,41 @@ def test_sharded_block_equals_unsharded(world, exchange, groups):
         assert torch.allclose(full, ref, rtol=1e-5, atol=1e-5), (rank, (full - ref).abs().max())
 
 
+def _tiny_worker(rank, world, port, q, exchange, n):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x, w, mod, cos, sin = make_case()
+        a, b = blk.shard_rows(n, world, rank)
+        spec = blk.ShardSpec(a, b, n, dist.group.WORLD, world, rank)
+        block = blk.DiTBlock(HEADS, HD, linear=dense, kv_exchange=exchange, ops=tops.TorchOps())
+        y = block(x[a:b].clone(), w, mod, [(0, b - a, 0)] if b > a else [], cos[a:b], sin[a:b], spec)
+        q.put((rank, blk.gather_rows(y, spec)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("exchange", ["overlap", "ring", "gather"])
+def test_fewer_tokens_than_ranks(exchange):
+    """2 tokens on 3 ranks: one rank owns no rows (its key set is empty, weight 0 in the merges)."""
+    world, n = 3, 2
+    x, w, mod, cos, sin = make_case()
+    ref = blk.DiTBlock(HEADS, HD, linear=dense, ops=tops.TorchOps())(x[:n].clone(), w, mod, [(0, n, 0)], cos[:n], sin[:n])
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_tiny_worker, args=(r, world, port, q, exchange, n)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=90) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, full in res:
+        assert torch.isfinite(full).all()
+        assert torch.allclose(full, ref, rtol=1e-5, atol=1e-5), (rank, (full - ref).abs().max())
+
+
 def test_shard_rows_cover_everything():
     for total in (0, 1, 7, 59440):
         for world in (1, 2, 3, 8):
@@ -98,3 +136,89 @@ def test_shard_rows_cover_everything():
             assert spans[0][0] == 0 and spans[-1][1] == total
             assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
             assert max(b - a for a, b in spans) - min(b - a for a, b in spans) <= 1
+
+
+def _post(q, item):
+    """Send `item` and flush it to the parent before the caller's os._exit (a queue's feeder thread dies with it)."""
+    q.put(item)
+    q.close()
+    q.join_thread()
+
+
+def _dead_rank_worker(rank, world, port, q, leave_after):
+    """Runs sharded blocks; rank `world - 1` leaves (exits without a word) after `leave_after` blocks.  The survivors
+    must see their next collective fail within the process group's short timeout instead of waiting for ever."""
+    import time
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=4))
+    x, w, mod, cos, sin = make_case()
+    a, b = blk.shard_rows(S, world, rank)
+    spec = blk.ShardSpec(a, b, S, dist.group.WORLD, world, rank)
+    block = blk.DiTBlock(HEADS, HD, linear=dense, ops=tops.TorchOps())
+    y = x[a:b].clone()
+    t0 = time.monotonic()
+    for i in range(3):
+        if rank == world - 1 and i == leave_after:
+            _post(q, (rank, "left", None, 0.0))
+            os._exit(0)  # between blocks: no collective of this rank is in flight
+        try:
+            y = block(y, w, mod, _segments(a, b), cos[a:b], sin[a:b], spec)
+        except Exception as e:  # the survivor's K/V all-gather of block `i`
+            _post(q, (rank, "raised", f"{type(e).__name__}: {str(e)[:200]}", time.monotonic() - t0))
+            os._exit(0)
+    _post(q, (rank, "finished", None, time.monotonic() - t0))
+    os._exit(0)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_a_rank_that_leaves_between_blocks_makes_the_others_raise(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_dead_rank_worker, args=(r, world, port, q, 1)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, what, err, t = q.get(timeout=120)
+        res[rank] = (what, err, t)
+    for p in procs:
+        p.join(timeout=60)
+        if p.exitcode is None:
+            p.kill()
+        assert p.exitcode == 0
+    assert res[world - 1][0] == "left"
+    for r in range(world - 1):
+        what, err, t = res[r]
+        assert what == "raised", res
+        assert t < 60, res  # bounded by the process group's 4 s timeout (plus the blocks already run), not a hang
+
+
+def _never_joins_worker(rank, world, port, q):
+    import time
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    t0 = time.monotonic()
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+        _post(q, (rank, "joined", None, time.monotonic() - t0))
+    except Exception as e:
+        _post(q, (rank, "raised", f"{type(e).__name__}: {str(e)[:200]}", time.monotonic() - t0))
+    os._exit(0)
+
+
+def test_a_rank_that_never_joins_makes_the_others_time_out():
+    """World size 2, only rank 0 starts: its rendezvous gives up after the short timeout with an error."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_never_joins_worker, args=(0, 2, _port(), q))
+    p.start()
+    rank, what, err, t = q.get(timeout=120)
+    p.join(timeout=60)
+    if p.exitcode is None:
+        p.kill()
+    assert what == "raised", (what, err)
+    assert t < 60

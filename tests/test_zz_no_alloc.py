@@ -19,17 +19,31 @@ DEV = torch.device("cuda")
 MAXREL_TOL = 1e-2  # the output tolerance the parity tests use
 
 
-def _noalloc(qa, xs, w, bias, out_dtype):
+def _gemm(entry, qa, xs, w, bias, out_dtype, quant_mode="ck", with_sch=True):
+    """One call of h3b_w4a8_gemm_noalloc ("noalloc") or of the allocating h3b_w4a8_gemm ("alloc", with a workspace
+    from torch) on the same arguments.  out_dtype torch.int32 asks for the raw accumulator (xs, s_ch, bias unused:
+    with_sch=False passes null pointers for them, as a C caller may)."""
     a = ql._WeightArgs(w)
     m = qa.shape[0]
     out = torch.empty(m, a.n, dtype=out_dtype, device=DEV)
+    code = _lib.INT32 if out_dtype == torch.int32 else _lib.act_code(out_dtype)
     b = None if bias is None else bias.to(device=DEV, dtype=out_dtype).contiguous()
-    rc = _lib.lib().h3b_w4a8_gemm_noalloc(qa.data_ptr(), qa.stride(0), xs.data_ptr(), m, a.q.data_ptr(), a.ldq,
-                                          a.s.data_ptr(), a.s_dtype, a.lds, a.s_ch.data_ptr(), a.cb.data_ptr(), a.group,
-                                          _lib.ptr(b), out.data_ptr(), _lib.act_code(out_dtype), a.n, a.n, a.k, 0,
-                                          _lib.stream_ptr(DEV))
-    _lib.check(rc, "h3b_w4a8_gemm_noalloc")
+    xs_p = xs.data_ptr() if with_sch else None
+    sch_p = a.s_ch.data_ptr() if with_sch else None
+    args = (qa.data_ptr(), qa.stride(0), xs_p, m, a.q.data_ptr(), a.ldq, a.s.data_ptr(), a.s_dtype, a.lds, sch_p,
+            a.cb.data_ptr(), a.group, _lib.ptr(b), out.data_ptr(), code, a.n, a.n, a.k, _lib.QMODE[quant_mode])
+    L = _lib.lib()
+    if entry == "noalloc":
+        _lib.check(L.h3b_w4a8_gemm_noalloc(*args, _lib.stream_ptr(DEV)), "h3b_w4a8_gemm_noalloc")
+    else:
+        nbytes = L.h3b_gemm_workspace_bytes(m, a.n, a.k)
+        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=DEV)
+        _lib.check(L.h3b_w4a8_gemm(*args, ws.data_ptr(), ws.numel(), _lib.stream_ptr(DEV)), "h3b_w4a8_gemm")
     return out
+
+
+def _noalloc(qa, xs, w, bias, out_dtype):
+    return _gemm("noalloc", qa, xs, w, bias, out_dtype)
 
 
 def _case(m, k, n, seed, out_dtype, with_bias):
@@ -58,6 +72,30 @@ def test_noalloc_matches_the_allocating_entry_point_on_two_calls_in_a_row():
     _check(*_case(129, 13824, 1500, seed=2, out_dtype=torch.float32, with_bias=False))
     # and call 1 again, after call 2 left its rows behind
     _check(*first)
+
+
+@pytest.mark.parametrize("quant_mode", ["ck", "eager"])
+def test_noalloc_matches_in_both_quant_modes(quant_mode):
+    """The eager epilogue (acc * (xs * s_ch)) as well as ck, over three slabs of decoded rows (K = 13824: 1184 rows per
+    slab, N = 3000), twice in a row."""
+    qa, xs, w, bias, _ = _case(200, 13824, 3000, seed=3, out_dtype=torch.bfloat16, with_bias=True)
+    for _ in range(2):
+        got = _gemm("noalloc", qa, xs, w, bias, torch.bfloat16, quant_mode)
+        want = _gemm("alloc", qa, xs, w, bias, torch.bfloat16, quant_mode)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+
+
+def test_noalloc_int32_accumulator_over_several_slabs_without_scales():
+    """int32 output (the raw accumulator; no xs, s_ch or bias given) over four slabs (K = 5120: 3264 rows per slab,
+    N = 10000), compared with the allocating entry point, twice in a row."""
+    qa, xs, w, _, _ = _case(130, 5120, 10000, seed=4, out_dtype=torch.int32, with_bias=False)
+    for _ in range(2):
+        got = _gemm("noalloc", qa, xs, w, None, torch.int32, with_sch=False)
+        want = _gemm("alloc", qa, xs, w, None, torch.int32, with_sch=False)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+        assert int(got.abs().max()) > 0
 
 
 def test_noalloc_refuses_rows_wider_than_its_scratch():
