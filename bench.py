@@ -44,7 +44,11 @@ MS = [256, 2048, 16384, 65536]
 METRIC = "W4A8 qlinear int8 TOPS"
 WORKLOADS = ("sweep", "block", "stream", "longseq")
 # (K, N, M) -> DRAM bytes read + written by that point's GEMM launch (ncu, one capture of the sweep's launches)
-GEMM_DRAM_BYTES = {}
+GEMM_DRAM_BYTES = {(5120, 5120, 256): 14888704, (5120, 5120, 2048): 36763648 + 3584,
+                   (5120, 5120, 16384): 196773376 + 148476928, (5120, 13824, 256): 37905664,
+                   (5120, 13824, 2048): 87693824 + 23752704, (5120, 13824, 16384): 359327232 + 421472000,
+                   (13824, 5120, 256): 40112640, (13824, 5120, 2048): 155125504 + 8532992,
+                   (13824, 5120, 16384): 1393123328 + 172492800}
 HID, HEADS, HEAD_DIM, FFN = 5120, 40, 128, 13824  # DiT width, attention heads x head dim, SwiGLU width
 BLOCK_LINEARS = [(HID, 3 * HID), (HID, HID), (HID, 2 * FFN), (FFN, HID)]  # (K, N): qkv, out, fc1, fc2 (SwiGLU input)
 BLOCK_OPS_PER_TOKEN = sum(2.0 * k * n for k, n in BLOCK_LINEARS)  # 634.4 M
@@ -349,9 +353,6 @@ def run_reference(args, rank):
             times.append(time.perf_counter() - t0)
     t_step = statistics.median(times)
     value = ops_of(sample) / t_step / 1e12
-    # the full sweep at the same per-token rate (every call decodes its weight, so small M runs slower and large M
-    # faster than this): context only, not measured
-    extrap = ops_of(sweep_points(args.ms)) / (t_step * sum(m for m in args.ms) / rows / 1.0) / 1e12
     cuda = None
     if staged is not None and not args.no_ref_cuda:
         try:
@@ -368,10 +369,7 @@ def run_reference(args, rank):
             "config": config_dict(args.ms, args.gpus),
             "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": kind,
                              "sample": f"each step: the three sweep projections at M = {rows} tokens (points of the sweep), "
-                                       f"timed as executed with {cores} threads: {what}",
-                             "extrapolated_full_sweep_tops": extrap,
-                             "extrapolation": "per token from the sample (the reference decodes the weight on every "
-                                              "call: context only, not measured)"},
+                                       f"timed as executed with {cores} threads: {what}"},
             "reference_cuda_path": cuda,
             "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

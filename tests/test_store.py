@@ -54,8 +54,7 @@ def test_layout_alignment_and_contiguous_blocks(written):
             a, b = f.block_range(i)
             assert b - a == f.block_nbytes and a % st.BLOCK_ALIGN == 0
             assert f.block_tensor(i).numel() == f.block_nbytes
-        g = f.load_globals("cpu")
-        assert g.video_patch_w.shape == (256, 16) and g.refiner == []
+        assert f.tensor("video_patch_proj.weight").shape == (256, 16)
 
 
 def test_block_views_into_a_device_style_buffer(written):
@@ -93,3 +92,20 @@ def test_failed_write_leaves_no_file(tmp_path):
     with pytest.raises(st.H3TError, match="block 0"):
         write_h3t(tmp_path / "bad.h3t", CFG, tensors)
     assert not (tmp_path / "bad.h3t").exists() and not (tmp_path / "bad.h3t.part").exists()
+
+
+@pytest.mark.parametrize("case", ["fp8_g16", "fp16_g128"])
+def test_writer_output_is_byte_identical_to_the_reference_writer(case, tmp_path):
+    """tests/golden/h3t_golden.json holds the size and sha256 of the file the REFERENCE writer produced from these same
+    seeded tensors (tests/golden/make_h3t_golden.py)."""
+    import hashlib
+    from pathlib import Path
+
+    gold = json.loads((Path(__file__).resolve().parent / "golden" / "h3t_golden.json").read_text())[case]
+    cfg = H3Config(hidden=256, layers=3, refiner_layers=0, heads=2, head_dim=128, ffn=512, text_dim=64, video_channels=4,
+                   audio_channels=8, quant_group=gold["group"])
+    path = tmp_path / f"{case}.h3t"
+    write_h3t(path, cfg, synthetic_store_tensors(cfg, group=gold["group"], scale_dtype=gold["format"], seed=gold["seed"]))
+    raw = path.read_bytes()
+    assert len(raw) == gold["size"]
+    assert hashlib.sha256(raw).hexdigest() == gold["sha256"]
