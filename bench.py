@@ -560,7 +560,7 @@ class PhaseProbe:
         return exch, attn
 
 
-def dit_measure(workload, steps, warmup, rank, world, local, group, kv_exchange="overlap", kv_groups=1, e2e=True,
+def dit_measure(workload, steps, warmup, rank, world, local, group, kv_exchange="gather", kv_groups=1, e2e=True,
                 check_rows=0):
     """Configs 3 and 5 on the kernels: DiT blocks on a video + audio sequence, token-sharded over `world` ranks (keys
     and values exchanged per block, the final hidden states all-gathered at the sequence boundary).  Times `steps`
@@ -648,6 +648,22 @@ def dit_measure(workload, steps, warmup, rank, world, local, group, kv_exchange=
            "linear_tops_per_rank": nb * rows * BLOCK_OPS_PER_TOKEN / (lin_ms * 1e-3) / 1e12 if lin_ms > 0 else None,
            "attention_tflops_per_rank": nb * 4.0 * rows * tokens * HEADS * HEAD_DIM / (attn_ms * 1e-3) / 1e12
            if attn_ms > 0 else None}
+    if world > 1:  # the link this exchange runs on: one all-gather of a K/V-sized shard, alone, best of 5
+        shard = torch.empty(rows, 2 * HEADS * HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        full = torch.empty(world * rows, 2 * HEADS * HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        best = float("inf")
+        for _ in range(6):
+            barrier()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            dist.all_gather_into_tensor(full, shard, group=group)
+            g1.record(stream)
+            barrier()
+            best = min(best, max_over_ranks(g0.elapsed_time(g1)))
+        rec["allgather_probe"] = {"bytes_in_per_rank": kv_bytes, "ms": best,
+                                  "gbs_in_per_rank": kv_bytes / (best * 1e-3) / 1e9,
+                                  "what": "one NCCL all_gather_into_tensor of this rank's keys+values shard, alone"}
+        del shard, full
     if check_rows and world > 1:
         idx = torch.linspace(0, tokens - 1, check_rows, device=dev).round().long()
         got = out[idx].float()
@@ -657,8 +673,10 @@ def dit_measure(workload, steps, warmup, rank, world, local, group, kv_exchange=
             y = x_all.clone()
             for i in range(nb):
                 y = ref_block(y, weights[i], mods[i], segs1, cos1, sin1)
-            want = y[idx].float()
+            want, x_in = y[idx].float(), x_all[idx].float()
             rec["check"] = {"rows": check_rows, "max_rel": float((got - want).abs().max() / want.abs().max()),
+                            "rel_l2_of_update": float((got - want).norm() / (want - x_in).norm()),
+                            "bit_identical": bool(torch.equal(got, want)),
                             "vs": "the same rows of the whole sequence recomputed on rank 0 alone (one GPU, no exchange)"}
             del y, x_all
         barrier()
@@ -913,7 +931,7 @@ def main():
                     help="sweep: config 2 (default); block: config 3; stream: config 4; longseq: config 5")
     ap.add_argument("--store-dir", default="", help="stream workload: directory for the temporary ~7.9 GB h3t store")
     ap.add_argument("--kv-groups", type=int, default=1, help="block/longseq over several GPUs: head groups of the K/V all-gather")
-    ap.add_argument("--kv-exchange", default="overlap", choices=["overlap", "gather", "ring"],
+    ap.add_argument("--kv-exchange", default="gather", choices=["gather", "overlap", "ring"],
                     help="DiT blocks on several GPUs: keys/values exchanged point-to-point behind the local attention "
                          "(overlap), all-gathered first (gather), or passed round a ring")
     ap.add_argument("--dit-steps", type=int, default=5, help="sweep line: timed forwards of the config-5 record (config 3: twice as many)")

@@ -98,7 +98,7 @@ int h3b_rms_modulate(const void* x, int x_dtype, int64_t ldx, int64_t M, int hid
 /* RMSNorm + AdaLN modulation fused into the rotate+quantise kernel: the codes and scales of h = _scale_shift_(_rms(x))
  * (model.py:64-66, 106-109, 239-241) without writing h; the activation side of the qkv and fc1 linears of a block.
  * Bit-identical to h3b_rms_modulate (bf16) followed by h3b_rotq on its output.  Every tensor bf16:
- *   x          [M, K], rows ldx elements apart; K a multiple of 512, at most 6144; convrot 256
+ *   x          [M, K], rows ldx elements apart; K a multiple of 256, at most 6144; convrot 256
  *   w          [K] norm weight (the reference rounds it to x's dtype first)
  *   shift      [n_rows, K] dt(shift);  scale1: [n_rows, K] dt(1 + dt(scale)), the factor _scale_shift_ multiplies by;
  *              rows ldm elements apart

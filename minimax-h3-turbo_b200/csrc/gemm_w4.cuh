@@ -12,6 +12,8 @@
 //   full[s]    A bytes (TMA) + one arrival per decoder warp: the stage is ready for the MMA
 //   empty[s]   the MMAs of stage s finished (tcgen05.commit): A, B and the packed tile may be refilled
 // Formats: scales fp16 / bf16 / fp32 with group 128, or fp8 e4m3 with group 16 (the benchmark and checkpoint formats).
+#pragma once
+
 #include "decode.cuh"
 #include "gemm_sm100.cuh"
 

@@ -1,0 +1,513 @@
+// Kernel KB, small-M form: the W4A8 GEMM for M <= 256 tokens, int4 weight decoded in the producer warps, K split
+// across CTAs so that every SM works although N / BN weight tiles alone would leave many idle.
+//
+// At small M the weight dominates the bytes and every output tile needs the whole K: one CTA per (N tile) gives
+// 20-108 CTAs for N = 5120-13824 on 148 SMs, each walking all of K.  Here a work unit is (N tile, K range): CTA u owns
+// output columns [BN nt, BN nt + BN) for ALL M rows (up to two 128-row subtiles, so each weight tile is decoded once)
+// and the k-blocks [kb0, kb1) of split s.  Integer partial sums are exact, so splitting K changes no bit of the result.
+//
+//   warp 0      TMA producer of the packed int4 weight tiles (BN x 64 bytes per k-block) into a deep ring (P ring)
+//   warp 6      TMA producer of the activation-code tiles (MS x 128 x 128 bytes per k-block) into the AB ring
+//   warps 7..   decoders: a P stage -> the BN x 128 int8 B tile of an AB stage (level tables + byte permutes, exactly
+//               decode.cuh's levels, 128-byte swizzle), then fence.proxy.async and an arrival per warp
+//   warp 1      MMA issuer: per k-block and M subtile 4 x tcgen05.mma.kind::i8 (K = 32 each) into its TMEM accumulator
+//   warps 2-5   epilogue: with one split, tcgen05.ld -> the W4A8 epilogue (as gemm_sm100.cuh) -> the output; with
+//               several, the raw int32 partial sums -> part[s][m][n] in the caller's workspace, and a second kernel
+//               (w4s_reduce_kernel, launched as a programmatic dependent so its launch overlaps this grid's tail) adds
+//               the splits in a fixed order and applies the epilogue.
+// The P ring is separate from (and deeper than) the AB ring, so weight bytes keep streaming from HBM while the tensor
+// core works on earlier k-blocks.  One work unit per CTA; every wait bounded (h3b_common.cuh).
+#pragma once
+
+#include "decode.cuh"
+#include "gemm_sm100.cuh"
+#include "gemm_w4.cuh"
+
+namespace h3b {
+
+// Epilogue parameters, runtime values: one kernel instantiation serves every output dtype, quant mode and bias choice.
+struct W4sEpi {
+  const float* xs;     // [M] per-row activation scales (unused for int32 output)
+  const float* sch;    // [N] per-channel weight scales
+  const void* bias;    // [N] of the output dtype, or null
+  void* out;           // [M, ldo] output
+  int64_t ldo;
+  int out_dtype;       // H3B_BF16 / H3B_FP16 / H3B_FP32 / H3B_INT32
+  int qmode;           // H3B_QMODE_CK / H3B_QMODE_EAGER
+  int32_t* part;       // [splits][M][N] partial sums (splits > 1), else null
+};
+
+template <int BN, int MS>
+struct W4sCfg {
+  // 16-weight chunks per decoder thread per k-block: 16 decoder warps for BN 128 and 256, 12 for 192 -- enough warps
+  // per scheduler to hide the shared-memory and permute latencies of the decode behind each other
+  static constexpr int CPT = BN == 128 ? 2 : 4;
+  static constexpr int DWARPS = BN * 8 / (32 * CPT);  // decoder warps (a thread owns CPT chunks of one B row)
+  static constexpr int LA = 4;                        // k-blocks of group scales each decoder thread loads ahead
+  static constexpr int A_BYTES = BM * BK;             // one 128-row activation subtile of one k-block
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int P_BYTES = BN * (BK / 2);
+  static constexpr int AB_BYTES = MS * A_BYTES + B_BYTES;
+  static constexpr int BUDGET = 210 * 1024;
+  static constexpr int AB_STAGES = (BUDGET * 3 / 4) / AB_BYTES < 2 ? 2 : ((BUDGET * 3 / 4) / AB_BYTES > 4 ? 4 : (BUDGET * 3 / 4) / AB_BYTES);
+  static constexpr int P_STAGES = (BUDGET - AB_STAGES * AB_BYTES) / P_BYTES > 10 ? 10 : (BUDGET - AB_STAGES * AB_BYTES) / P_BYTES;
+  static constexpr int TMEM_COLS = MS * BN <= 128 ? 128 : (MS * BN <= 256 ? 256 : 512);
+  static constexpr int THREADS = 32 * (7 + DWARPS);
+  static_assert(AB_STAGES * MS * A_BYTES >= 4 * 32 * 33 * 4, "the epilogue's transpose squares live in the activation ring");
+  static constexpr int SMEM = 1024 + AB_STAGES * AB_BYTES + P_STAGES * P_BYTES + 4096 + 512;
+  static constexpr uint32_t IDESC = idesc_i8(BM, BN);
+  static_assert(P_STAGES >= 2 && CPT * 32 * DWARPS == BN * 8 && 8 % CPT == 0, "bad small-M GEMM configuration");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// The W4A8 epilogue of `n` (<= 8) consecutive accumulators of one row, runtime dtype / mode (the same operations, in the
+// same order, as epilogue_row32: (fp32(acc) * xs) * s_ch or fp32(acc) * (xs * s_ch), rounded to the output dtype, then
+// + bias and a second rounding), stored at column n0 of `orow`.
+__device__ __forceinline__ void w4s_store8(const int32_t (&a)[8], int n, float xsr, const W4sEpi& e, char* orow, int64_t n0,
+                                           bool vec) {
+  if (e.out_dtype == H3B_INT32) {
+    int32_t* o = reinterpret_cast<int32_t*>(orow) + n0;
+    if (vec) {
+      reinterpret_cast<int4*>(o)[0] = make_int4(a[0], a[1], a[2], a[3]);
+      reinterpret_cast<int4*>(o)[1] = make_int4(a[4], a[5], a[6], a[7]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < n) o[j] = a[j];
+    }
+    return;
+  }
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float s = j < n ? __ldg(e.sch + n0 + j) : 0.f;
+    const float f = __int2float_rn(a[j]);
+    v[j] = e.qmode == H3B_QMODE_CK ? __fmul_rn(__fmul_rn(f, xsr), s) : __fmul_rn(f, __fmul_rn(xsr, s));
+  }
+  if (e.out_dtype == H3B_FP32) {
+    if (e.bias) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < n) v[j] = __fadd_rn(v[j], static_cast<const float*>(e.bias)[n0 + j]);
+    }
+    float* o = reinterpret_cast<float*>(orow) + n0;
+    if (vec) {
+      reinterpret_cast<float4*>(o)[0] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < n) o[j] = v[j];
+    }
+    return;
+  }
+  const bool bf = e.out_dtype == H3B_BF16;
+  uint16_t h[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float r = bf ? __bfloat162float(__float2bfloat16_rn(v[j])) : __half2float(__float2half_rn(v[j]));
+    if (e.bias && j < n) {
+      const float b = bf ? __bfloat162float(static_cast<const __nv_bfloat16*>(e.bias)[n0 + j])
+                         : __half2float(static_cast<const __half*>(e.bias)[n0 + j]);
+      r = __fadd_rn(r, b);
+    }
+    if (bf) {
+      const __nv_bfloat16 t = __float2bfloat16_rn(r);
+      h[j] = *reinterpret_cast<const uint16_t*>(&t);
+    } else {
+      const __half t = __float2half_rn(r);
+      h[j] = *reinterpret_cast<const uint16_t*>(&t);
+    }
+  }
+  uint16_t* o = reinterpret_cast<uint16_t*>(orow) + n0;
+  if (vec) {
+    *reinterpret_cast<uint4*>(o) = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                                              h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < n) o[j] = h[j];
+  }
+}
+
+template <int BN, int MS, int SDT>
+__global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
+    gemm_w4s_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
+                    const void* __restrict__ s_rel, int64_t lds, const float* __restrict__ codebook, const W4sEpi epi,
+                    int M, int N, int K, int splits) {
+  using C = W4sCfg<BN, MS>;
+  constexpr int GROUP = SDT == H3B_FP8_E4M3 ? 16 : 128;
+  extern __shared__ __align__(1024) unsigned char w4s_smem[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(w4s_smem) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem;                                    // [AB_STAGES][MS][A_BYTES]
+  unsigned char* sB = sA + C::AB_STAGES * MS * C::A_BYTES;     // [AB_STAGES][B_BYTES]
+  unsigned char* sP = sB + C::AB_STAGES * C::B_BYTES;          // [P_STAGES][P_BYTES]
+  uint4* lut = reinterpret_cast<uint4*>(sP + C::P_STAGES * C::P_BYTES);  // fp8: the 256 level tables
+  uint64_t* pkfull = reinterpret_cast<uint64_t*>(lut + 256);
+  uint64_t* pkempty = pkfull + C::P_STAGES;
+  uint64_t* afull = pkempty + C::P_STAGES;
+  uint64_t* bfull = afull + C::AB_STAGES;
+  uint64_t* empty = bfull + C::AB_STAGES;
+  uint64_t* tfull = empty + C::AB_STAGES;
+  uint64_t* mdone = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int nt = blockIdx.x % n_tiles, split = blockIdx.x / n_tiles;  // CTAs of one split share the activation rows
+  const int num_kb = (K + BK - 1) / BK;
+  const int kb0 = static_cast<int>(static_cast<int64_t>(split) * num_kb / splits);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * num_kb / splits);
+  const int nkb = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::P_STAGES; ++s) {
+      mbar_init(&pkfull[s], 1);
+      mbar_init(&pkempty[s], C::DWARPS);
+    }
+    for (int s = 0; s < C::AB_STAGES; ++s) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&bfull[s], C::DWARPS);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(mdone, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  float cb[16];
+  if (warp >= 7) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) cb[i] = __ldg(codebook + i);
+    if constexpr (SDT == H3B_FP8_E4M3) {
+      for (int b = threadIdx.x - 224; b < 256; b += 32 * C::DWARPS) lut[b] = level_table(cb, fp8e4m3_to_f32(static_cast<uint32_t>(b)));
+    }
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmP);
+    pdl_launch_dependents();  // the reduction kernel may be scheduled now; it waits for this grid to finish
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ------------------------------------------------------ packed weight tiles -> P ring
+      int ps = 0;
+      uint32_t ph = 0;
+      int fills = 0;
+      for (int i = 0; i < nkb; ++i) {
+        if (!mbar_wait(&pkempty[ps], ph ^ 1u, abort_flag)) break;
+        mbar_arrive_expect_tx(&pkfull[ps], C::P_BYTES);
+        tma_load_2d(sP + ps * C::P_BYTES, &tmP, &pkfull[ps], (kb0 + i) * (BK / 2), nt * BN);
+        ++fills;
+        if (++ps == C::P_STAGES) { ps = 0; ph ^= 1u; }
+      }
+      for (int j = fills > C::P_STAGES ? fills - C::P_STAGES : 0; j < fills; ++j)  // drain this CTA's own copies
+        if (!mbar_wait_drain(&pkfull[j % C::P_STAGES], static_cast<uint32_t>((j / C::P_STAGES) & 1))) break;
+    }
+  } else if (warp == 6) {
+    if (lane == 0) {  // ------------------------------------------------------ activation tiles -> AB ring
+      int as = 0;
+      uint32_t ph = 0;
+      int fills = 0;
+      for (int i = 0; i < nkb; ++i) {
+        if (!mbar_wait(&empty[as], ph ^ 1u, abort_flag)) break;
+        mbar_arrive_expect_tx(&afull[as], MS * C::A_BYTES);
+#pragma unroll
+        for (int ms = 0; ms < MS; ++ms)
+          tma_load_2d(sA + (as * MS + ms) * C::A_BYTES, &tmA, &afull[as], (kb0 + i) * BK, ms * BM);
+        ++fills;
+        if (++as == C::AB_STAGES) { as = 0; ph ^= 1u; }
+      }
+      for (int j = fills > C::AB_STAGES ? fills - C::AB_STAGES : 0; j < fills; ++j)
+        if (!mbar_wait_drain(&afull[j % C::AB_STAGES], static_cast<uint32_t>((j / C::AB_STAGES) & 1))) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ------------------------------------------------------ MMA issuer
+      int as = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int i = 0; i < nkb && ok; ++i) {
+        if (!mbar_wait(&afull[as], ph, abort_flag) || !mbar_wait(&bfull[as], ph, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t b0 = smem_u32(sB + as * C::B_BYTES);
+#pragma unroll
+        for (int ms = 0; ms < MS; ++ms) {
+          const uint32_t a0 = smem_u32(sA + (as * MS + ms) * C::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k)
+            mma_i8(tmem_base + static_cast<uint32_t>(ms * BN), smem_desc_sw128(a0 + 32 * k), smem_desc_sw128(b0 + 32 * k),
+                   C::IDESC, (i | k) != 0);
+        }
+        mma_commit(&empty[as]);
+        if (++as == C::AB_STAGES) { as = 0; ph ^= 1u; }
+      }
+      if (ok) mma_commit(tfull);
+      mma_commit(mdone);
+      mbar_wait_drain(mdone, 0);
+    }
+  } else if (warp < 6) {  // ------------------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    const bool ok = mbar_wait(tfull, 0, abort_flag);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      if (splits > 1) {
+        // raw int32 partial sums of this split -> part[split][m][n], coalesced: each warp's 32 rows x 32 columns go
+        // through a padded shared-memory square (the activation ring is free: every MMA has completed), and every
+        // store instruction then writes 32 consecutive columns of one row
+        int32_t* sq = reinterpret_cast<int32_t*>(sA) + quad * (32 * 33);
+        int32_t* pbase = epi.part + static_cast<int64_t>(split) * M * N;
+#pragma unroll 1
+        for (int ms = 0; ms < MS; ++ms) {
+          const int row0 = ms * BM + quad * 32;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ms * BN + c * 32), r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sq[lane * 33 + j] = static_cast<int32_t>(r[j]);
+            __syncwarp();
+            const int64_t n = static_cast<int64_t>(nt) * BN + c * 32 + lane;
+            for (int rr = 0; rr < 32; ++rr) {
+              const int row = row0 + rr;
+              if (row < M && n < N) pbase[static_cast<int64_t>(row) * N + n] = sq[rr * 33 + lane];
+            }
+            __syncwarp();
+          }
+        }
+      } else {
+        const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
+        const bool vec_ok = (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
+#pragma unroll 1
+        for (int ms = 0; ms < MS; ++ms) {
+          const int row = ms * BM + quad * 32 + lane;
+          const float xsr = (epi.out_dtype != H3B_INT32 && row < M) ? epi.xs[row] : 0.f;
+          char* orow = static_cast<char*>(epi.out) + static_cast<size_t>(row) * static_cast<size_t>(epi.ldo) * osz;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ms * BN + c * 32), r);
+            tmem_ld_wait();
+            const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 32;
+            if (row < M && n0 < N) {
+              const int ncols = N - n0 < 32 ? static_cast<int>(N - n0) : 32;
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                const int nn = ncols - 8 * g;
+                if (nn <= 0) break;
+                int32_t a[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) a[q] = static_cast<int32_t>(r[8 * g + q]);
+                w4s_store8(a, nn < 8 ? nn : 8, xsr, epi, orow, n0 + 8 * g, vec_ok && nn >= 8);
+              }
+            }
+          }
+        }
+      }
+    }
+  } else {  // -------------------------------------------------------------------------------------- decoders
+    const int dt = threadIdx.x - 224;             // 0 .. 32 DWARPS - 1
+    const int r_loc = (dt * C::CPT) >> 3;         // this thread's row of the B tile
+    const int j0 = (dt * C::CPT) & 7;             // its first 16-weight chunk in the row
+    const int n = nt * BN + r_loc;
+    const bool row_ok = n < N;
+    const unsigned char* srow = static_cast<const unsigned char*>(s_rel) +
+                                static_cast<int64_t>(row_ok ? n : 0) * lds * (SDT == H3B_FP8_E4M3 ? 1 : (SDT == H3B_FP32 ? 4 : 2));
+    // this thread's group scales of k-block i: the one scale of its row (group-128 formats, as a float) or the scale
+    // byte of each of its chunks (fp8 group 16); plain global loads, issued LA k-blocks before their use
+    auto load_scales = [&](int i, float& g, uint32_t (&f8)[C::CPT]) {
+      const int64_t kbase = static_cast<int64_t>(kb0 + i) * BK;
+      if constexpr (SDT == H3B_FP8_E4M3) {
+#pragma unroll
+        for (int c = 0; c < C::CPT; ++c) {
+          const int64_t e0 = kbase + 16 * (j0 + c);
+          f8[c] = (row_ok && i < nkb && e0 < K) ? static_cast<uint32_t>(srow[e0 / GROUP]) : 0u;
+        }
+      } else {
+        const int64_t e0 = kbase + 16 * j0;
+        g = (row_ok && i < nkb && e0 < K) ? scale_at<SDT>(srow, e0 / GROUP) : 0.f;
+      }
+    };
+    float sg[C::LA];
+    uint32_t s8[C::LA][C::CPT];
+#pragma unroll
+    for (int u = 0; u < C::LA; ++u) {
+      sg[u] = 0.f;
+#pragma unroll
+      for (int c = 0; c < C::CPT; ++c) s8[u][c] = 0u;
+      load_scales(u, sg[u], s8[u]);
+    }
+    int ps = 0, as = 0;
+    uint32_t pph = 0, aph = 0;
+    bool ok = true;
+    for (int i0 = 0; i0 < nkb && ok; i0 += C::LA) {
+#pragma unroll
+      for (int u = 0; u < C::LA; ++u) {  // unrolled, so the scale ring stays in registers
+        const int i = i0 + u;
+        if (i >= nkb) break;
+        if (!mbar_wait(&pkfull[ps], pph, abort_flag) || !mbar_wait(&empty[as], aph ^ 1u, abort_flag)) { ok = false; break; }
+        uint4 t = make_uint4(0, 0, 0, 0);
+        if constexpr (SDT != H3B_FP8_E4M3) t = level_table(cb, sg[u]);
+        const unsigned char* prow = sP + ps * C::P_BYTES + r_loc * (BK / 2);
+        unsigned char* brow = sB + as * C::B_BYTES + r_loc * BK;
+#pragma unroll
+        for (int c = 0; c < C::CPT; ++c) {
+          const int j = j0 + c;
+          if constexpr (SDT == H3B_FP8_E4M3) t = lut[s8[u][c]];
+          const uint2 pk = *reinterpret_cast<const uint2*>(prow + 8 * j);
+          const uint2 lo = decode8(pk.x, t), hi = decode8(pk.y, t);
+          *reinterpret_cast<uint4*>(brow + ((j ^ (r_loc & 7)) << 4)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+        fence_proxy_async_smem();  // the tensor core reads these bytes through the async proxy
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bfull[as]);
+          mbar_arrive(&pkempty[ps]);
+        }
+        if (++ps == C::P_STAGES) { ps = 0; pph ^= 1u; }
+        if (++as == C::AB_STAGES) { as = 0; aph ^= 1u; }
+        load_scales(i + C::LA, sg[u], s8[u]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// Sum of the splits' int32 partial sums, in split order, then the W4A8 epilogue; one thread per 8 output columns.
+// Launched as a programmatic dependent of gemm_w4s_kernel: it waits for that grid (and its memory) before reading.
+static __global__ void __launch_bounds__(256) w4s_reduce_kernel(const W4sEpi epi, int M, int N, int splits) {
+  pdl_wait_primary();
+  const int vpr = (N + 7) / 8;
+  const int64_t total = static_cast<int64_t>(M) * vpr;
+  const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
+  const bool vec_ok = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(epi.part) & 15) == 0 &&
+                      (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(v / vpr);
+    const int64_t n0 = (v - static_cast<int64_t>(row) * vpr) * 8;
+    const int nn = N - n0 < 8 ? static_cast<int>(N - n0) : 8;
+    int32_t a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int s = 0; s < splits; ++s) {
+      const int32_t* p = epi.part + (static_cast<int64_t>(s) * M + row) * N + n0;
+      if (vec_ok && nn == 8) {
+        const int4 x = __ldcs(reinterpret_cast<const int4*>(p)), y = __ldcs(reinterpret_cast<const int4*>(p) + 1);
+        a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w; a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j < nn) a[j] += p[j];
+      }
+    }
+    const float xsr = epi.out_dtype == H3B_INT32 ? 0.f : epi.xs[row];
+    char* orow = static_cast<char*>(epi.out) + static_cast<size_t>(row) * static_cast<size_t>(epi.ldo) * osz;
+    w4s_store8(a, nn, xsr, epi, orow, n0, vec_ok && nn == 8);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host side
+// The work split: all M rows per CTA (MS subtiles), then the N tile width and the number of K splits that give the
+// shortest estimated time -- one wave of at most `sms` CTAs, each doing ceil(num_kb / S) k-blocks of MS x BN x 128 x
+// 128 MACs, plus (S > 1) writing and re-reading S x M x N int32 partial sums through L2 and the reduction's launch.
+struct W4sPlan {
+  int bn, ms, splits;
+};
+
+inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, int sms) {
+  const int ms = M <= BM ? 1 : 2;
+  const int64_t num_kb = (K + BK - 1) / BK;
+  W4sPlan best{128, ms, 1};
+  double best_t = -1;
+  for (int bn : {256, 192, 128}) {
+    const int64_t n_tiles = (N + bn - 1) / bn;
+    for (int s = 1; s <= 16 && s <= num_kb; ++s) {
+      const int64_t units = n_tiles * s;
+      const int64_t waves = (units + sms - 1) / sms;
+      if (waves > 1 && s > 1) break;
+      const double mma = static_cast<double>(waves) * ((num_kb + s - 1) / s) * ms * bn * 2.0;  // tensor clocks per CTA
+      const double decode = static_cast<double>(waves) * ((num_kb + s - 1) / s) * (ms == 1 ? 1.2 : 0.6) * bn;
+      const double red = s > 1 ? 2.0 * s * M * N * 4 / 8192.0 + 3000.0 : 0.0;  // ~8 KB per clock of L2, + a launch
+      const double t = (mma > decode ? mma : decode) + 2500.0 + red;           // + pipeline fill and epilogue
+      if (best_t < 0 || t < best_t) {
+        best_t = t;
+        best = W4sPlan{bn, ms, s};
+      }
+    }
+  }
+  return best;
+}
+
+inline size_t w4s_partial_bytes(int64_t M, int64_t N, int splits) {
+  return splits > 1 ? static_cast<size_t>(splits) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4 : 0;
+}
+
+template <int BN, int MS, int SDT>
+static int w4s_launch_cfg(int splits, const CUtensorMap& ta, const CUtensorMap& tp, const void* s_rel, int64_t lds,
+                          const float* codebook, const W4sEpi& epi, int M, int N, int K, cudaStream_t st) {
+  using C = W4sCfg<BN, MS>;
+  auto kern = gemm_w4s_kernel<BN, MS, SDT>;
+  static std::atomic<unsigned long long> attr_done{0};  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_done.load() & bit)) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm w4s)");
+    attr_done.fetch_or(bit);
+  }
+  const int units = ((N + BN - 1) / BN) * splits;
+  kern<<<units, C::THREADS, C::SMEM, st>>>(ta, tp, s_rel, lds, codebook, epi, M, N, K, splits);
+  return check_launch("gemm_w4s_kernel");
+}
+
+// The small-M GEMM of one scale dtype: the main kernel, then (splits > 1) the reduction as a programmatic dependent.
+template <int SDT>
+int w4s_launch_sdt(const W4sPlan& plan, const int8_t* a, int64_t lda, const void* q4, int64_t ldq4, const void* s_rel,
+                   int64_t lds, const float* codebook, const W4sEpi& epi, int M, int N, int K, cudaStream_t st) {
+  CUtensorMap ta, tp;
+  int rc = make_map(&ta, a, K, M, lda, BM);
+  if (rc) return rc;
+  rc = make_map_packed(&tp, q4, K / 2, N, ldq4, plan.bn);
+  if (rc) return rc;
+#define H3B_W4S(B, S) if (plan.bn == B && plan.ms == S) rc = w4s_launch_cfg<B, S, SDT>(plan.splits, ta, tp, s_rel, lds, codebook, epi, M, N, K, st); else
+  H3B_W4S(256, 2) H3B_W4S(192, 2) H3B_W4S(128, 2) H3B_W4S(256, 1) H3B_W4S(192, 1) H3B_W4S(128, 1)
+  return fail(H3B_ERR_ARG, "small-M GEMM: unsupported tile plan");
+#undef H3B_W4S
+  if (rc || plan.splits == 1) return rc;
+  cudaLaunchConfig_t cfg = {};
+  int sms = num_sms();
+  const int64_t vecs = static_cast<int64_t>(M) * ((N + 7) / 8);
+  const int64_t want = (vecs + 255) / 256;
+  cfg.gridDim = dim3(static_cast<unsigned>(want < 4ll * sms ? want : 4ll * sms), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, w4s_reduce_kernel, epi, M, N, plan.splits);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(w4s_reduce_kernel)");
+  return check_launch("w4s_reduce_kernel");
+}
+
+}  // namespace h3b

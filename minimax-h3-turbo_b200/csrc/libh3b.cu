@@ -199,7 +199,7 @@ int h3b_rotq_rms_modulate(const void* x, int64_t M, int64_t K, int64_t ldx, cons
                           const int32_t* token_rows, int convrot, int quant_mode, int8_t* q, int64_t ldq, float* xs,
                           void* stream) {
   if (M < 0 || K <= 0 || !rotq_rmsmod_supported(K))
-    return fail(H3B_ERR_ARG, "rotq_rms_modulate: K must be a positive multiple of 512, at most 6144");
+    return fail(H3B_ERR_ARG, "rotq_rms_modulate: K must be a positive multiple of 256, at most 6144");
   if (convrot != 256) return fail(H3B_ERR_UNSUPPORTED, "rotq_rms_modulate: convrot must be 256");
   if (quant_mode != H3B_QMODE_CK && quant_mode != H3B_QMODE_EAGER) return fail(H3B_ERR_ARG, "quant_mode must be 'ck' or 'eager'");
   if (M == 0) return H3B_OK;
@@ -283,8 +283,9 @@ int h3b_int8_gemm_s32(const int8_t* a, int64_t lda, int64_t M, const int8_t* b, 
 }
 
 size_t h3b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  (void)M;
-  return round_up(static_cast<size_t>(N) * static_cast<size_t>(K), 256);  // the decoded int8 grid
+  const size_t grid = static_cast<size_t>(N) * static_cast<size_t>(K);  // the decoded int8 grid (separate decode pass)
+  const size_t part = w4_workspace_bytes(M, N, K);                      // split-K partial sums (small-M kernel)
+  return round_up(grid > part ? grid : part, 256);
 }
 
 size_t h3b_linear_workspace_bytes(int64_t M, int64_t N, int64_t K) {

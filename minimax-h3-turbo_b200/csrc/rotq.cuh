@@ -533,8 +533,8 @@ __global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __
 }
 
 // ------------------------------------------------------------------------------------------------ warp-per-row kernel
-// bf16 activations, ConvRot 256, K a multiple of 512, quantise modes.  One warp owns a whole row.  Pass p transforms
-// chunk pair c = 32 p + lane (lane 0 at column 16 c, lane 1 at K/2 + 16 c) exactly as rotq_kernel's split mode does,
+// bf16 activations, ConvRot 256, K a multiple of 256, quantise modes.  One warp owns a whole row.  Pass p transforms
+// chunk pair c = 32 p + lane (lane 0 at column 16 c, lane 1 at rowk_off(K) + 16 c) like rotq_kernel's split mode,
 // keeps dt(y) as bf16 pairs in the warp's row buffer in shared memory (64 bytes per thread per pass, so 2 K bytes per
 // row) and the running absmax in a register.  After the last pass a warp shuffle gives the row's amax, and a second
 // sweep over the buffer quantises and stores.  No CTA barrier: each warp runs its rows on its own, and the per-row
@@ -554,20 +554,26 @@ __host__ __device__ constexpr int rowk_xbytes() { return 2 * xgrp(16) * 8; }  //
 // transform's column writes (16 threads, element t + 16 i) and the quantiser's row reads (thread t', 16-byte chunks of
 // row t') are both free of bank conflicts.
 constexpr int ROWK_BLOCK_WORDS = 16 * 16 + 16;
+// A thread's two lanes are the same row, `rowk_off(K)` elements apart: K / 2 when K is a multiple of 512, otherwise
+// (K a multiple of 256 only, e.g. the official width 5376 = 21 x 256) half a ConvRot block more, so that both lanes sit
+// at the same position of their blocks; the upper lane then runs off the end of the row for the last 128 elements of
+// the lower half, where it loads zeros (no effect on the transform of other blocks or on the absmax) and stores nothing.
+__host__ __device__ constexpr int64_t rowk_off(int64_t K) { return (K + 511) / 512 * 256; }
+__host__ __device__ constexpr int rowk_passes(int64_t K) { return static_cast<int>((2 * rowk_off(K) + ROWK_PASS - 1) / ROWK_PASS); }
 __host__ __device__ inline size_t rowk_warp_bytes(int64_t K) {
-  return static_cast<size_t>((K + ROWK_PASS - 1) / ROWK_PASS) * (2 * ROWK_BLOCK_WORDS * 4) + rowk_xbytes();
+  return static_cast<size_t>(rowk_passes(K)) * (2 * ROWK_BLOCK_WORDS * 4) + rowk_xbytes();
 }
 __device__ __forceinline__ int rowk_word(int i, int col) { return 16 * i + 4 * ((col >> 2) ^ ((i >> 1) & 3)) + (col & 3); }
 
 
 // 16 bf16 values from element e of a bf16 array (16-byte aligned) for lane 0 and from element e + off for lane 1, as
-// (lane 0, lane 1) pairs
-__device__ __forceinline__ void load_pairs16(const __nv_bfloat16* p, int64_t e, int64_t off, float2 (&out)[16]) {
+// (lane 0, lane 1) pairs; lane 1 reads zeros when e + off is past the row (hi_ok false)
+__device__ __forceinline__ void load_pairs16(const __nv_bfloat16* p, int64_t e, int64_t off, bool hi_ok, float2 (&out)[16]) {
   const uint4* a = reinterpret_cast<const uint4*>(p + e);
   const uint4* b = reinterpret_cast<const uint4*>(p + e + off);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const uint4 ua = __ldg(a + i), ub = __ldg(b + i);
+    const uint4 ua = __ldg(a + i), ub = hi_ok ? __ldg(b + i) : make_uint4(0u, 0u, 0u, 0u);
     const uint32_t wa[4] = {ua.x, ua.y, ua.z, ua.w}, wb[4] = {ub.x, ub.y, ub.z, ub.w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -587,21 +593,34 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
   constexpr float SCALE = 0.0625f;
   extern __shared__ __align__(16) unsigned char rotq_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int P = (K + ROWK_PASS - 1) / ROWK_PASS;
-  const int nchunk = K / 32;  // chunk pairs per row; a multiple of 16, so a pass is full or its upper half-warp idles
+  const int64_t half = rowk_off(K);  // lane 1's offset from lane 0 (K / 2 when K is a multiple of 512)
+  const int P = rowk_passes(K);
+  const int nchunk = static_cast<int>(half / 16);  // chunk pairs per row; a multiple of 16, so a pass is full or its
+                                                   // upper half-warp idles
   unsigned char* wbase = rotq_smem + static_cast<size_t>(warp) * rowk_warp_bytes(K);
   const int t = lane & 15;
   // this half-warp's block in the row buffer of pass 0 (passes are 2 blocks apart)
   uint32_t* bblk = reinterpret_cast<uint32_t*>(wbase + rowk_xbytes()) + (lane >> 4) * ROWK_BLOCK_WORDS;
   float2* gbuf = reinterpret_cast<float2*>(wbase) + (lane >> 4) * xgrp(16);
-  const int64_t half = K / 2;
   const int64_t rstep = static_cast<int64_t>(gridDim.x) * nw;
   int64_t row = static_cast<int64_t>(blockIdx.x) * nw + warp;
 
   Raw<DT, SW> raw;
   auto load = [&](int64_t r, int p) {  // r < M; the idle half-warp of a row's last pass re-reads chunk nchunk - 1
     const int c = 32 * p + lane;
-    load_raw<DT, SW, true>(raw, x, ldx, r, M, 16ll * (c < nchunk ? c : nchunk - 1), K);
+    const int64_t e = 16ll * (c < nchunk ? c : nchunk - 1);
+    const char* base = static_cast<const char*>(x) + static_cast<size_t>(r) * static_cast<size_t>(ldx) * 2;
+#pragma unroll
+    for (int h = 0; h < (SW ? 2 : 1); ++h) {  // SwiGLU rows hold [gate | up], K elements apart
+      const uint4* lo = reinterpret_cast<const uint4*>(base + static_cast<size_t>(e + h * K) * 2);
+      const uint4* hi = reinterpret_cast<const uint4*>(base + static_cast<size_t>(e + half + h * K) * 2);
+      const bool hi_ok = e + half < K;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        raw.u[h * 2 + i] = __ldg(lo + i);
+        raw.u[((SW ? 2 : 1) + h) * 2 + i] = hi_ok ? __ldg(hi + i) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
   };
   // the four swizzled column offsets of this thread's element column t (row i uses colw[(i >> 1) & 3])
   int colw[4];
@@ -672,15 +691,16 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
       else if (row + rstep < M) load(row + rstep, 0);
       if constexpr (NORM) {  // x -> h: n = dt((x rs) w); h = dt(dt(n s1) + sh) for a modulated token
         const int64_t e = 16ll * ((32 * p + lane) < nchunk ? 32 * p + lane : nchunk - 1);
+        const bool hi_ok = e + half < K;
         float2 a[16];
-        load_pairs16(nrm.w, e, half, a);
+        load_pairs16(nrm.w, e, half, hi_ok, a);
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = rnd_bf16x2(__fmul2_rn(__fmul2_rn(v[i], RS2), a[i]));
         if (mrow >= 0) {
-          load_pairs16(nrm.scale1 + mrow * nrm.ldm, e, half, a);
+          load_pairs16(nrm.scale1 + mrow * nrm.ldm, e, half, hi_ok, a);
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = rnd_bf16x2(__fmul2_rn(v[i], a[i]));
-          load_pairs16(nrm.shift + mrow * nrm.ldm, e, half, a);
+          load_pairs16(nrm.shift + mrow * nrm.ldm, e, half, hi_ok, a);
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = rnd_bf16x2(__fadd2_rn(v[i], a[i]));
         }
@@ -759,7 +779,7 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
       const int c = 32 * p + lane;
       if (c < nchunk) {
         *reinterpret_cast<uint4*>(qrow + 16ll * c) = make_uint4(wA[0], wA[1], wA[2], wA[3]);
-        *reinterpret_cast<uint4*>(qrow + half + 16ll * c) = make_uint4(wB[0], wB[1], wB[2], wB[3]);
+        if (half + 16ll * c < K) *reinterpret_cast<uint4*>(qrow + half + 16ll * c) = make_uint4(wB[0], wB[1], wB[2], wB[3]);
       }
     }
   }
@@ -863,7 +883,7 @@ static int launch_split(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t
                         int ydt, int64_t ldy, cudaStream_t st) {
   constexpr int G = CR >= 256 ? 16 : (CR == 64 ? 4 : 1);
   if constexpr (DT == DT_BF16 && CR == 256 && MODE != MODE_ROTATE) {
-    if (K % 512 == 0 && M >= ROWK_MIN_ROWS && rowk_warp_bytes(K) <= ROWK_MAX_WARP_BYTES && rowk_enabled())
+    if (K % 256 == 0 && M >= ROWK_MIN_ROWS && rowk_warp_bytes(K) <= ROWK_MAX_WARP_BYTES && rowk_enabled())
       return rowk_launch<MODE, SW>(x, ldx, M, K, q, ldq, xs, st);
   }
   if constexpr (DT != DT_FP32) {
@@ -905,14 +925,14 @@ int rotq_launch(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, i
                 : launch_dt<MODE_EAGER, false>(x_dtype, convrot, x, ldx, M, K, q, ldq, xs, y, y_dtype, ldy, st);
 }
 
-// RMSNorm + modulation fused into the quantiser (bf16 x, ConvRot 256, K a multiple of 512 and <= 6144: the shapes the
+// RMSNorm + modulation fused into the quantiser (bf16 x, ConvRot 256, K a multiple of 256 and <= 6144: the shapes the
 // norm's warp-per-row kernel serves, whose sum order this reproduces).  Codes and scales are bit-identical to
 // rms_modulate_launch followed by rotq_launch on its output.
-bool rotq_rmsmod_supported(int64_t K) { return K > 0 && K % 512 == 0 && K <= 6144; }
+bool rotq_rmsmod_supported(int64_t K) { return K > 0 && K % 256 == 0 && K <= 6144; }
 
 int rotq_rmsmod_launch(const void* x, int64_t ldx, int64_t M, int64_t K, const RowNorm& nrm, int mode, int8_t* q,
                        int64_t ldq, float* xs, cudaStream_t st) {
-  if (!rotq_rmsmod_supported(K)) return fail(H3B_ERR_UNSUPPORTED, "rotq_rms_modulate: K must be a multiple of 512, at most 6144");
+  if (!rotq_rmsmod_supported(K)) return fail(H3B_ERR_UNSUPPORTED, "rotq_rms_modulate: K must be a multiple of 256, at most 6144");
   if (mode == MODE_CK) return rowk_launch<MODE_CK, false, true>(x, ldx, M, K, q, ldq, xs, st, nrm);
   if (mode == MODE_EAGER) return rowk_launch<MODE_EAGER, false, true>(x, ldx, M, K, q, ldq, xs, st, nrm);
   return fail(H3B_ERR_ARG, "rotq_rms_modulate: quant_mode must be ck or eager");

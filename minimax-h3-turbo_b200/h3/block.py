@@ -17,11 +17,13 @@ tensors: there is no CPU path.  (The token-sharding tests run the same block on 
 operator set, written with the reference's torch formulas, as `ops=`.)
 
 Token sharding (rank r of P owns a contiguous slice of rows): every op above is token-wise except attention, which needs
-all keys and values.  kv_exchange "overlap" (the default) sends this rank's keys and values to every other rank and
-receives theirs (NCCL point-to-point, one batched group) while the local queries attend to the local keys; one attention
-call over the received keys follows, and the two partial results are merged by their log-sum-exps (h3b_attn_merge).
-"gather" all-gathers K and V first and makes one attention call; "ring" passes the shards round the ranks.
-`gather_rows` assembles the final hidden states at the sequence boundary.
+all keys and values.  kv_exchange "gather" (the default) all-gathers K and V and makes one attention call over all
+keys: every query sees exactly what it would see on one GPU, so the sharded block is bit-identical to the unsharded one.
+"overlap" sends this rank's keys and values to every other rank and receives theirs (NCCL point-to-point, one batched
+group) while the local queries attend to the local keys; one attention call over the received keys follows, and the two
+partial results are merged by their log-sum-exps (h3b_attn_merge) -- the exchange hides behind 1/P of the attention,
+at the price of two attention calls and results that differ from one call in the last bits.  "ring" passes the shards
+round the ranks.  `gather_rows` assembles the final hidden states at the sequence boundary.
 """
 from __future__ import annotations
 
@@ -126,9 +128,9 @@ class Prenorm:
 def prenorm_codes(pre: Prenorm, convrot: int = 256, quant_mode: str = "ck") -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
     """(int8 codes [M, K], fp32 scales [M, 1]) of h = pre.materialize() from the fused kernel (h3b_rotq_rms_modulate),
     bit-identical to quantising the materialised h; None where that kernel does not apply (not bf16 CUDA rows, K not a
-    multiple of 512 or above 6144, ConvRot other than 256)."""
+    multiple of 256 or above 6144, ConvRot other than 256)."""
     x = pre.x
-    if not (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] % 512 == 0 and x.shape[1] <= 6144
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] % 256 == 0 and x.shape[1] <= 6144
             and convrot == 256):
         return None
     from .. import _lib
@@ -411,22 +413,22 @@ def overlap_attention(q: torch.Tensor, kv: torch.Tensor, spec: ShardSpec, ops=KE
     return merger.add(o, lse, last=True)
 
 
-KV_EXCHANGES = ("overlap", "gather", "ring")
+KV_EXCHANGES = ("gather", "overlap", "ring")
 
 
 class DiTBlock:
     """Runs H3 DiT blocks on the W4A8 kernels.  heads / head_dim / eps as in H3Config.
 
-    kv_exchange (token-sharded runs): "overlap" (default; keys and values exchanged point-to-point while the local
-    queries attend to the local keys, then one call over the received keys and a log-sum-exp merge), "gather" (one
-    all-gather of K and V, optionally in `kv_groups` head groups, then one attention call) or "ring" (shards passed
-    round the ranks, one attention call and merge per shard).  `ops`: the operator set (KernelOps; tests of the
+    kv_exchange (token-sharded runs): "gather" (default: one all-gather of K and V, optionally in `kv_groups` head
+    groups, then one attention call; bit-identical to one GPU), "overlap" (keys and values exchanged point-to-point
+    while the local queries attend to the local keys, then one call over the received keys and a log-sum-exp merge) or
+    "ring" (shards passed round the ranks, one attention call and merge per shard).  `ops`: the operator set (KernelOps; tests of the
     sharding plumbing on CPU ranks pass the reference's torch formulas).  `probe(tag)`, when given, is called on the
     host at the phase boundaries of the attention ("qk_ready", "local_done", "kv_ready", "attn_done") so a caller can
     record CUDA events there."""
 
     def __init__(self, heads: int, head_dim: int, norm_eps: float = 1e-5, qk_norm_eps: float = 1e-5,
-                 precision: str = "a8", attn_chunk: Optional[int] = None, linear=None, kv_exchange: str = "overlap",
+                 precision: str = "a8", attn_chunk: Optional[int] = None, linear=None, kv_exchange: str = "gather",
                  fuse_norm: Optional[bool] = None, kv_groups: int = 1, ops=None,
                  probe: Optional[Callable[[str], None]] = None):
         if kv_exchange not in KV_EXCHANGES:

@@ -10,12 +10,15 @@ import torch  # noqa: E402
 from minimax_h3_turbo_b200.h3 import qlinear as ql  # noqa: E402
 
 DEV = torch.device("cuda")
-CASES = [  # (M, K, quant mode, SwiGLU input): bf16, ConvRot 256, M >= 4096, K <= 5120 a multiple of 512 (the row kernel)
+CASES = [  # (M, K, quant mode, SwiGLU input): bf16, ConvRot 256, M >= 4096, K <= 5120 a multiple of 256 (the row kernel)
     (4096, 5120, "ck", False),
     (4133, 3072, "eager", False),   # M not a multiple of the warps of a CTA
     (4096, 2560, "ck", True),       # the last pass of a row is half a warp
     (4500, 512, "ck", False),       # one half-warp pass per row
     (4096, 1536, "eager", True),
+    (4096, 3840, "ck", False),      # K = 15 x 256, not a multiple of 512: the upper lane runs off the row end
+    (4133, 1280, "eager", True),    # the same with a SwiGLU input
+    (4096, 256, "ck", False),       # one ConvRot block: the upper lane has nothing at all
 ]
 
 

@@ -36,7 +36,11 @@ def _check(pre, mode="ck"):
 
 @pytest.mark.parametrize("m,k,mdt,mode", [(4096, 5120, torch.float32, "ck"), (4133, 5120, torch.bfloat16, "eager"),
                                           (37, 5120, torch.float32, "ck"), (1, 1536, torch.bfloat16, "ck"),
-                                          (1000, 512, torch.float16, "eager"), (300, 6144, torch.float32, "ck")])
+                                          (1000, 512, torch.float16, "eager"), (300, 6144, torch.float32, "ck"),
+                                          # the official H3 width 5376 = 21 x 256 and other widths that are not
+                                          # multiples of 512
+                                          (4096, 5376, torch.float32, "ck"), (777, 5376, torch.bfloat16, "eager"),
+                                          (2000, 768, torch.bfloat16, "ck"), (129, 256, torch.float32, "ck")])
 def test_fused_codes_equal_norm_then_quantise(m, k, mdt, mode):
     x, w, sh, sc = _inputs(m, k, mdt, seed=m + k)
     segs = [(0, m // 2, 0), (m // 2, max(m // 2, m - 3), 2)]  # the last tokens: no modulation
@@ -55,10 +59,10 @@ def test_fused_codes_with_per_token_rows_and_without_modulation():
 
 
 def test_shapes_outside_the_fused_kernel_fall_back():
-    x, w, sh, sc = _inputs(64, 768, torch.float32, seed=9)
+    x, w, sh, sc = _inputs(64, 6400, torch.float32, seed=9)
     pre = blk.Prenorm(x, w, 1e-5, sh, sc, [(0, 64, 0)])
-    assert blk.prenorm_codes(pre) is None  # K = 768: not a multiple of 512
-    wt = synthetic_w4a8(256, 768, seed=1, device=DEV)
+    assert blk.prenorm_codes(pre) is None  # K = 6400: wider than the fused kernel's row buffer allows
+    wt = synthetic_w4a8(256, 6400, seed=1, device=DEV)
     assert torch.equal(blk.prenorm_linear(pre, wt), ql.linear(pre.materialize(), wt))
 
 

@@ -1,4 +1,4 @@
-"""The warp-per-row rotate+quantise kernel (bf16, ConvRot 256, M >= 4096, K <= 5120 a multiple of 512) against the
+"""The warp-per-row rotate+quantise kernel (bf16, ConvRot 256, M >= 4096, K <= 5120 a multiple of 256) against the
 CTA-per-row-group kernel, bit for bit, and against the oracle: both quantiser modes, SwiGLU inputs, half-warp passes,
 ragged M and degenerate rows (zeros, a value near the bf16 maximum, subnormals only, an infinity)."""
 import os
@@ -35,7 +35,7 @@ def test_row_kernel_against_the_oracle():
     from oracle import qlinear_oracle as orc
     from minimax_h3_turbo_b200.h3 import qlinear as ql
 
-    for i in (0, 1, 3):  # the cases without SwiGLU (the oracle's exp comes from the host libm)
+    for i in (0, 1, 3, 5, 7):  # the cases without SwiGLU (the oracle's exp comes from the host libm)
         m, k, mode, _ = rotq_cases.CASES[i]
         x = rotq_cases.case_input(i)
         q, xs = ql._quantize_rows(x, 256, mode)
