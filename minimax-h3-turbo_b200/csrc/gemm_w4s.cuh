@@ -47,16 +47,20 @@ struct W4sCfg {
   static constexpr int A_BYTES = BM * BK;             // one 128-row activation subtile of one k-block
   static constexpr int B_BYTES = BN * BK;
   static constexpr int P_BYTES = BN * (BK / 2);
-  static constexpr int AB_BYTES = MS * A_BYTES + B_BYTES;
   static constexpr int BUDGET = 210 * 1024;
-  static constexpr int AB_STAGES = (BUDGET * 3 / 4) / AB_BYTES < 2 ? 2 : ((BUDGET * 3 / 4) / AB_BYTES > 4 ? 4 : (BUDGET * 3 / 4) / AB_BYTES);
-  static constexpr int P_STAGES = (BUDGET - AB_STAGES * AB_BYTES) / P_BYTES > 10 ? 10 : (BUDGET - AB_STAGES * AB_BYTES) / P_BYTES;
+  // Three rings.  The activation tiles come from L2 with a latency of a few microseconds when every SM streams at
+  // once, so their ring is the deepest the budget allows; the decoded weight tiles are produced in shared memory and
+  // need only double buffering; the packed weight tiles take the rest.
+  static constexpr int A_STAGES = MS == 1 ? 6 : (BN == 128 ? 4 : 3);
+  static constexpr int B_STAGES = MS == 1 && BN == 128 ? 3 : 2;
+  static constexpr int P_LEFT = (BUDGET - A_STAGES * MS * A_BYTES - B_STAGES * B_BYTES) / P_BYTES;
+  static constexpr int P_STAGES = P_LEFT > 10 ? 10 : P_LEFT;
   static constexpr int TMEM_COLS = MS * BN <= 128 ? 128 : (MS * BN <= 256 ? 256 : 512);
   static constexpr int THREADS = 32 * (7 + DWARPS);
-  static_assert(AB_STAGES * MS * A_BYTES >= 4 * 32 * 33 * 4, "the epilogue's transpose squares live in the activation ring");
-  static constexpr int SMEM = 1024 + AB_STAGES * AB_BYTES + P_STAGES * P_BYTES + 4096 + 512;
+  static constexpr int SMEM = 1024 + A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES + 4096 + 512;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
   static_assert(P_STAGES >= 2 && CPT * 32 * DWARPS == BN * 8 && 8 % CPT == 0, "bad small-M GEMM configuration");
+  static_assert(A_STAGES * MS * A_BYTES >= 4 * 32 * 33 * 4, "the epilogue's transpose squares live in the activation ring");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
@@ -137,28 +141,31 @@ template <int BN, int MS, int SDT>
 __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
     gemm_w4s_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
                     const void* __restrict__ s_rel, int64_t lds, const float* __restrict__ codebook, const W4sEpi epi,
-                    int M, int N, int K, int splits) {
+                    int M, int N, int K, int splits, int m_tiles) {
   using C = W4sCfg<BN, MS>;
   constexpr int GROUP = SDT == H3B_FP8_E4M3 ? 16 : 128;
   extern __shared__ __align__(1024) unsigned char w4s_smem[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(w4s_smem) + 1023) & ~uintptr_t(1023));
-  unsigned char* sA = smem;                                    // [AB_STAGES][MS][A_BYTES]
-  unsigned char* sB = sA + C::AB_STAGES * MS * C::A_BYTES;     // [AB_STAGES][B_BYTES]
-  unsigned char* sP = sB + C::AB_STAGES * C::B_BYTES;          // [P_STAGES][P_BYTES]
+  unsigned char* sA = smem;                                    // [A_STAGES][MS][A_BYTES]
+  unsigned char* sB = sA + C::A_STAGES * MS * C::A_BYTES;      // [B_STAGES][B_BYTES]
+  unsigned char* sP = sB + C::B_STAGES * C::B_BYTES;           // [P_STAGES][P_BYTES]
   uint4* lut = reinterpret_cast<uint4*>(sP + C::P_STAGES * C::P_BYTES);  // fp8: the 256 level tables
   uint64_t* pkfull = reinterpret_cast<uint64_t*>(lut + 256);
   uint64_t* pkempty = pkfull + C::P_STAGES;
   uint64_t* afull = pkempty + C::P_STAGES;
-  uint64_t* bfull = afull + C::AB_STAGES;
-  uint64_t* empty = bfull + C::AB_STAGES;
-  uint64_t* tfull = empty + C::AB_STAGES;
+  uint64_t* aempty = afull + C::A_STAGES;
+  uint64_t* bfull = aempty + C::A_STAGES;
+  uint64_t* bempty = bfull + C::B_STAGES;
+  uint64_t* tfull = bempty + C::B_STAGES;
   uint64_t* mdone = tfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = (N + BN - 1) / BN;
-  const int nt = blockIdx.x % n_tiles, split = blockIdx.x / n_tiles;  // CTAs of one split share the activation rows
+  // unit = (split, M tile, N tile), N fastest: the CTAs of one split and M tile run together and share activation rows
+  const int nt = blockIdx.x % n_tiles, mt = (blockIdx.x / n_tiles) % m_tiles, split = blockIdx.x / (n_tiles * m_tiles);
+  const int row_base = mt * MS * BM;  // first activation / output row of this CTA
   const int num_kb = (K + BK - 1) / BK;
   const int kb0 = static_cast<int>(static_cast<int64_t>(split) * num_kb / splits);
   const int kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * num_kb / splits);
@@ -169,10 +176,13 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
       mbar_init(&pkfull[s], 1);
       mbar_init(&pkempty[s], C::DWARPS);
     }
-    for (int s = 0; s < C::AB_STAGES; ++s) {
+    for (int s = 0; s < C::A_STAGES; ++s) {
       mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < C::B_STAGES; ++s) {
       mbar_init(&bfull[s], C::DWARPS);
-      mbar_init(&empty[s], 1);
+      mbar_init(&bempty[s], 1);
     }
     mbar_init(tfull, 1);
     mbar_init(mdone, 1);
@@ -217,31 +227,31 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
         if (!mbar_wait_drain(&pkfull[j % C::P_STAGES], static_cast<uint32_t>((j / C::P_STAGES) & 1))) break;
     }
   } else if (warp == 6) {
-    if (lane == 0) {  // ------------------------------------------------------ activation tiles -> AB ring
+    if (lane == 0) {  // ------------------------------------------------------ activation tiles -> A ring
       int as = 0;
       uint32_t ph = 0;
       int fills = 0;
       for (int i = 0; i < nkb; ++i) {
-        if (!mbar_wait(&empty[as], ph ^ 1u, abort_flag)) break;
+        if (!mbar_wait(&aempty[as], ph ^ 1u, abort_flag)) break;
         mbar_arrive_expect_tx(&afull[as], MS * C::A_BYTES);
 #pragma unroll
         for (int ms = 0; ms < MS; ++ms)
-          tma_load_2d(sA + (as * MS + ms) * C::A_BYTES, &tmA, &afull[as], (kb0 + i) * BK, ms * BM);
+          tma_load_2d(sA + (as * MS + ms) * C::A_BYTES, &tmA, &afull[as], (kb0 + i) * BK, row_base + ms * BM);
         ++fills;
-        if (++as == C::AB_STAGES) { as = 0; ph ^= 1u; }
+        if (++as == C::A_STAGES) { as = 0; ph ^= 1u; }
       }
-      for (int j = fills > C::AB_STAGES ? fills - C::AB_STAGES : 0; j < fills; ++j)
-        if (!mbar_wait_drain(&afull[j % C::AB_STAGES], static_cast<uint32_t>((j / C::AB_STAGES) & 1))) break;
+      for (int j = fills > C::A_STAGES ? fills - C::A_STAGES : 0; j < fills; ++j)
+        if (!mbar_wait_drain(&afull[j % C::A_STAGES], static_cast<uint32_t>((j / C::A_STAGES) & 1))) break;
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ------------------------------------------------------ MMA issuer
-      int as = 0;
-      uint32_t ph = 0;
+      int as = 0, bs = 0;
+      uint32_t aph = 0, bph = 0;
       bool ok = true;
       for (int i = 0; i < nkb && ok; ++i) {
-        if (!mbar_wait(&afull[as], ph, abort_flag) || !mbar_wait(&bfull[as], ph, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&afull[as], aph, abort_flag) || !mbar_wait(&bfull[bs], bph, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t b0 = smem_u32(sB + as * C::B_BYTES);
+        const uint32_t b0 = smem_u32(sB + bs * C::B_BYTES);
 #pragma unroll
         for (int ms = 0; ms < MS; ++ms) {
           const uint32_t a0 = smem_u32(sA + (as * MS + ms) * C::A_BYTES);
@@ -250,8 +260,10 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
             mma_i8(tmem_base + static_cast<uint32_t>(ms * BN), smem_desc_sw128(a0 + 32 * k), smem_desc_sw128(b0 + 32 * k),
                    C::IDESC, (i | k) != 0);
         }
-        mma_commit(&empty[as]);
-        if (++as == C::AB_STAGES) { as = 0; ph ^= 1u; }
+        mma_commit(&aempty[as]);  // both slots free once these MMAs complete
+        mma_commit(&bempty[bs]);
+        if (++as == C::A_STAGES) { as = 0; aph ^= 1u; }
+        if (++bs == C::B_STAGES) { bs = 0; bph ^= 1u; }
       }
       if (ok) mma_commit(tfull);
       mma_commit(mdone);
@@ -270,7 +282,7 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
         int32_t* pbase = epi.part + static_cast<int64_t>(split) * M * N;
 #pragma unroll 1
         for (int ms = 0; ms < MS; ++ms) {
-          const int row0 = ms * BM + quad * 32;
+          const int row0 = row_base + ms * BM + quad * 32;
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             uint32_t r[32];
@@ -292,7 +304,7 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
         const bool vec_ok = (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
 #pragma unroll 1
         for (int ms = 0; ms < MS; ++ms) {
-          const int row = ms * BM + quad * 32 + lane;
+          const int row = row_base + ms * BM + quad * 32 + lane;
           const float xsr = (epi.out_dtype != H3B_INT32 && row < M) ? epi.xs[row] : 0.f;
           char* orow = static_cast<char*>(epi.out) + static_cast<size_t>(row) * static_cast<size_t>(epi.ldo) * osz;
 #pragma unroll 1
@@ -349,19 +361,19 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
       for (int c = 0; c < C::CPT; ++c) s8[u][c] = 0u;
       load_scales(u, sg[u], s8[u]);
     }
-    int ps = 0, as = 0;
-    uint32_t pph = 0, aph = 0;
+    int ps = 0, bs = 0;
+    uint32_t pph = 0, bph = 0;
     bool ok = true;
     for (int i0 = 0; i0 < nkb && ok; i0 += C::LA) {
 #pragma unroll
       for (int u = 0; u < C::LA; ++u) {  // unrolled, so the scale ring stays in registers
         const int i = i0 + u;
         if (i >= nkb) break;
-        if (!mbar_wait(&pkfull[ps], pph, abort_flag) || !mbar_wait(&empty[as], aph ^ 1u, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&pkfull[ps], pph, abort_flag) || !mbar_wait(&bempty[bs], bph ^ 1u, abort_flag)) { ok = false; break; }
         uint4 t = make_uint4(0, 0, 0, 0);
         if constexpr (SDT != H3B_FP8_E4M3) t = level_table(cb, sg[u]);
         const unsigned char* prow = sP + ps * C::P_BYTES + r_loc * (BK / 2);
-        unsigned char* brow = sB + as * C::B_BYTES + r_loc * BK;
+        unsigned char* brow = sB + bs * C::B_BYTES + r_loc * BK;
 #pragma unroll
         for (int c = 0; c < C::CPT; ++c) {
           const int j = j0 + c;
@@ -373,11 +385,11 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
         fence_proxy_async_smem();  // the tensor core reads these bytes through the async proxy
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&bfull[as]);
+          mbar_arrive(&bfull[bs]);
           mbar_arrive(&pkempty[ps]);
         }
         if (++ps == C::P_STAGES) { ps = 0; pph ^= 1u; }
-        if (++as == C::AB_STAGES) { as = 0; aph ^= 1u; }
+        if (++bs == C::B_STAGES) { bs = 0; bph ^= 1u; }
         load_scales(i + C::LA, sg[u], s8[u]);
       }
     }
@@ -428,27 +440,33 @@ static __global__ void __launch_bounds__(256) w4s_reduce_kernel(const W4sEpi epi
 // shortest estimated time -- one wave of at most `sms` CTAs, each doing ceil(num_kb / S) k-blocks of MS x BN x 128 x
 // 128 MACs, plus (S > 1) writing and re-reading S x M x N int32 partial sums through L2 and the reduction's launch.
 struct W4sPlan {
-  int bn, ms, splits;
+  int bn, ms, splits;  // N tile, 128-row M subtiles per CTA (1: one CTA per M tile), K splits
 };
 
 inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, int sms) {
-  const int ms = M <= BM ? 1 : 2;
   const int64_t num_kb = (K + BK - 1) / BK;
-  W4sPlan best{128, ms, 1};
+  W4sPlan best{128, M <= BM ? 1 : 2, 1};
   double best_t = -1;
-  for (int bn : {256, 192, 128}) {
-    const int64_t n_tiles = (N + bn - 1) / bn;
-    for (int s = 1; s <= 16 && s <= num_kb; ++s) {
-      const int64_t units = n_tiles * s;
-      const int64_t waves = (units + sms - 1) / sms;
-      if (waves > 1 && s > 1) break;
-      const double mma = static_cast<double>(waves) * ((num_kb + s - 1) / s) * ms * bn * 2.0;  // tensor clocks per CTA
-      const double decode = static_cast<double>(waves) * ((num_kb + s - 1) / s) * (ms == 1 ? 1.2 : 0.6) * bn;
-      const double red = s > 1 ? 2.0 * s * M * N * 4 / 8192.0 + 3000.0 : 0.0;  // ~8 KB per clock of L2, + a launch
-      const double t = (mma > decode ? mma : decode) + 2500.0 + red;           // + pipeline fill and epilogue
-      if (best_t < 0 || t < best_t) {
-        best_t = t;
-        best = W4sPlan{bn, ms, s};
+  for (int ms : {1, 2}) {
+    if (ms == 2 && M <= BM) continue;
+    const int64_t m_tiles = ms == 1 ? (M + BM - 1) / BM : 1;
+    for (int bn : {256, 192, 128}) {
+      const int64_t n_tiles = (N + bn - 1) / bn;
+      const int a_stages = ms == 1 ? 6 : (bn == 128 ? 4 : 3);
+      for (int s = 1; s <= 16 && s <= num_kb; ++s) {
+        const int64_t units = m_tiles * n_tiles * s;
+        const int64_t waves = (units + sms - 1) / sms;
+        if (waves > 1 && s > 1) break;
+        // clocks per k-block: the tensor core (ms x bn x 2), the activation tile through L2 (~64 B/clock per SM), and
+        // the activation ring covering ~3000 clocks of load latency
+        const double mma = ms * bn * 2.0, afetch = ms * BM * BK / 64.0, lat = 3000.0 / a_stages;
+        const double t_kb = mma > afetch ? (mma > lat ? mma : lat) : (afetch > lat ? afetch : lat);
+        const double red = s > 1 ? 4000.0 + static_cast<double>(s) * M * N * 4 / 2048.0 : 0.0;
+        const double t = static_cast<double>(waves) * ((num_kb + s - 1) / s) * t_kb + 4000.0 + red;
+        if (best_t < 0 || t < best_t) {
+          best_t = t;
+          best = W4sPlan{bn, ms, s};
+        }
       }
     }
   }
@@ -473,8 +491,9 @@ static int w4s_launch_cfg(int splits, const CUtensorMap& ta, const CUtensorMap& 
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm w4s)");
     attr_done.fetch_or(bit);
   }
-  const int units = ((N + BN - 1) / BN) * splits;
-  kern<<<units, C::THREADS, C::SMEM, st>>>(ta, tp, s_rel, lds, codebook, epi, M, N, K, splits);
+  const int m_tiles = MS == 1 ? (M + BM - 1) / BM : 1;
+  const int units = ((N + BN - 1) / BN) * m_tiles * splits;
+  kern<<<units, C::THREADS, C::SMEM, st>>>(ta, tp, s_rel, lds, codebook, epi, M, N, K, splits, m_tiles);
   return check_launch("gemm_w4s_kernel");
 }
 

@@ -67,12 +67,13 @@ int gemm_w4_launch(const int8_t* a, int64_t lda, const void* q4, int64_t ldq4, c
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   if (w4s_enabled(M)) {
     W4sPlan plan = w4s_plan(M, N, K, num_sms());
-    // H3B_W4S_PLAN="bn,splits" in the environment replaces the planner's choice (read per call; for tile sweeps)
+    // H3B_W4S_PLAN="bn,splits,subtiles" in the environment replaces the planner's choice (read per call; for tile
+    // sweeps)
     if (const char* e = getenv("H3B_W4S_PLAN")) {
-      int bn = 0, sp = 0;
-      if (sscanf(e, "%d,%d", &bn, &sp) == 2 && (bn == 128 || bn == 192 || bn == 256) && sp >= 1 &&
-          sp <= static_cast<int>((K + BK - 1) / BK))
-        plan = W4sPlan{bn, plan.ms, sp};
+      int bn = 0, sp = 0, ms = 0;
+      if (sscanf(e, "%d,%d,%d", &bn, &sp, &ms) == 3 && (bn == 128 || bn == 192 || bn == 256) && sp >= 1 &&
+          sp <= static_cast<int>((K + BK - 1) / BK) && (ms == 1 || (ms == 2 && M <= 2 * BM)))
+        plan = W4sPlan{bn, ms, sp};
     }
     // fewer splits when the caller's workspace cannot hold the partial sums (int32 [splits, M, N], 16-byte aligned)
     const size_t per_split = static_cast<size_t>(M) * static_cast<size_t>(N) * 4;
