@@ -56,6 +56,7 @@ BLOCK_OPS_PER_TOKEN = sum(2.0 * k * n for k, n in BLOCK_LINEARS)  # 634.4 M
 SEQS = {"block": (31, 26, 15, 200, 1),  # 5 s 832x480: 12090 + 200 = 12290 tokens, one block
         "longseq": (241, 20, 12, 1600, 4)}  # 40 s 640x384: 57840 + 1600 = 59440 tokens, four blocks
 STREAM_BLOCKS, STREAM_TOKENS, STREAM_RESIDENT, STREAM_RING, STREAM_PREFETCH = 48, 4096, 4, 3, 2
+E2E_ROWS = 8192  # tokens per chunk of the end-to-end leg's pipeline
 
 
 def load_package():
@@ -934,6 +935,7 @@ def main():
     ap.add_argument("--kv-exchange", default="gather", choices=["gather", "overlap", "ring"],
                     help="DiT blocks on several GPUs: keys/values exchanged point-to-point behind the local attention "
                          "(overlap), all-gathered first (gather), or passed round a ring")
+    ap.add_argument("--no-official", action="store_true", help="sweep line: skip the official-geometry record")
     ap.add_argument("--dit-steps", type=int, default=5, help="sweep line: timed forwards of the config-5 record (config 3: twice as many)")
     ap.add_argument("--no-dit", action="store_true", help="sweep line: skip the config-5 (and, on one GPU, config-3) records")
     args = ap.parse_args()
@@ -952,6 +954,39 @@ def main():
         run_stream(args, rank, world, local)
         return
     run_sweep(args, rank, world, local)
+
+
+OFFICIAL = {"qkv": (5376, 21504, False), "out": (7168, 5376, False), "fc1": (5376, 28672, False),
+            "fc2": (14336, 5376, True)}  # (K, N, SwiGLU input): hidden 5376, 56 x 128 heads, FFN 14336
+
+
+def official_points(dev, ms=(256, 4096), reps=10):
+    """The four projections of the official H3 DiT (h3turbo/h3/config.py:12-31) in the real checkpoint format, one W4A8
+    linear each through qlinear.linear (device-resident bf16 activations), at M = 256 and 4096: CUDA-event time of
+    `reps` calls after 3 warm-up calls.  Context beside the headline sweep, not part of `value`."""
+    import torch
+    from minimax_h3_turbo_b200.h3 import qlinear as ql
+    from minimax_h3_turbo_b200.h3.synth import synthetic_activation, synthetic_w4a8_fp8
+
+    out = []
+    for name, (k, n, sw) in OFFICIAL.items():
+        w = synthetic_w4a8_fp8(n, k, seed=k + n, device=dev)
+        for m in ms:
+            x = synthetic_activation(m, 2 * k if sw else k, seed=m + k, device=dev)
+            act = "swiglu" if sw else None
+            for _ in range(3):
+                ql.linear(x, w, input_act=act)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                ql.linear(x, w, input_act=act)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            us = e0.elapsed_time(e1) / reps * 1e3
+            out.append({"proj": name, "K": k, "N": n, "M": m, "swiglu_input": sw, "us": round(us, 1),
+                        "tops": 2.0 * m * n * k / (us * 1e-6) / 1e12})
+        del w
+    return {"format": "fp8 e4m3 group-16 scales, 16-level codebook", "points": out}
 
 
 def measure_int8_peak(dev, n=8192, reps=10):
@@ -1114,22 +1149,28 @@ def run_sweep(args, rank, world, local):
         d2h = sum(m * n * 2 for (_, n, m) in points)
 
         # pipelined like a serving loop: host->device copies on one copy stream, device->host on another, compute on
-        # the current stream; two device input slots, so point i + 1 uploads while point i computes
+        # the current stream.  Each point goes through in chunks of at most E2E_ROWS tokens (the linear is token-wise,
+        # so a chunk is an exact sub-problem) over three device input slots, so the upload of chunk j + 1 and the
+        # download of chunk j - 1 run while chunk j computes: the host link, not the order of the copies, bounds it
+        kmax = max(k for (k, _, _) in points)
+        chunks = [(i, k, n, r0, min(m, r0 + E2E_ROWS)) for i, (k, n, m) in enumerate(points) for r0 in range(0, m, E2E_ROWS)]
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        dbuf = [torch.empty(big_in, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-        slot_free = [None, None]  # compute-done event of the point that last read each slot
+        nslot = 3
+        dbuf = [torch.empty(min(big_in, E2E_ROWS * kmax), dtype=torch.bfloat16, device=dev) for _ in range(nslot)]
+        slot_free = [None] * nslot  # compute-done event of the chunk that last read each slot
 
         def e2e_step():
-            for i, (k, n, m) in enumerate(points):
+            for j, (i, k, n, r0, r1) in enumerate(chunks):
                 w, _ = weights[(k, n)]
-                slot = i % 2
-                xd = dbuf[slot][: m * k].view(m, k)
+                slot = j % nslot
+                rows = r1 - r0
+                xd = dbuf[slot][: rows * k].view(rows, k)
                 if slot_free[slot] is None:
                     s_in.wait_stream(stream)
                 else:
                     s_in.wait_event(slot_free[slot])
                 with torch.cuda.stream(s_in):
-                    xd.copy_(hin[: m * k].view(m, k), non_blocking=True)
+                    xd.copy_(hin[r0 * k: r1 * k].view(rows, k), non_blocking=True)
                     ready = torch.cuda.Event()
                     ready.record(s_in)
                 stream.wait_event(ready)
@@ -1139,7 +1180,7 @@ def run_sweep(args, rank, world, local):
                 slot_free[slot] = done
                 s_out.wait_event(done)
                 with torch.cuda.stream(s_out):
-                    hout[: m * n].view(m, n).copy_(y, non_blocking=True)
+                    hout[r0 * n: r1 * n].view(rows, n).copy_(y, non_blocking=True)
                 y.record_stream(s_out)
             stream.wait_stream(s_out)  # the step ends when its last result is in host memory
 
@@ -1176,6 +1217,9 @@ def run_sweep(args, rank, world, local):
     # ---- a measured int8 denominator beside 2 x bf16: cuBLASLt's int8 GEMM (torch._int_mm) at 8192^3, best of 10
     int8_lib = measure_int8_peak(dev)
 
+    # ---- the official H3 geometry in the real checkpoint format (fp8 e4m3 group-16 scales), through qlinear.linear
+    official = None if args.no_official else official_points(dev)
+
     # ---- the DiT records: config 5 token-sharded over the N ranks (every N), config 3 on one GPU
     del weights, grids, acts, outs, codes, xs
     torch.cuda.empty_cache()
@@ -1208,7 +1252,7 @@ def run_sweep(args, rank, world, local):
                                   "unit": "GB/s", "frac": rotq_gbs / pk["hbm_gbs"]},
                 "kernel_ms_per_step": tot, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "gpu_launches": sum(2 if fused[p] else 3 for p in points) * args.steps,
-                "sharded_block": sharded, "block": block3}
+                "sharded_block": sharded, "block": block3, "official": official}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

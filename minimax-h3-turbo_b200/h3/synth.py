@@ -46,6 +46,21 @@ def synthetic_w4a8(n: int, k: int, *, group: int = 128, convrot: int = 256, seed
 
 
 @torch.no_grad()
+def synthetic_w4a8_fp8(n: int, k: int, *, seed: int = 0, device="cuda") -> W4A8Weight:
+    """A seeded layer in the real checkpoints' format (h3turbo/h3/types.py:10-47): random 4-bit codebook indices, fp8
+    e4m3 group scales per 16 weights drawn from [20, 200] (so |level| reaches the +-127 clamp), a 16-level codebook in
+    [-1, 1] and fp32 per-channel scales -- the shape of the reference's own test weights (tests/test_h3_qlinear.py:46-53)."""
+    if k % 256:
+        raise ValueError("K must be a multiple of 256 (the ConvRot block)")
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randint(-128, 128, (n, k // 2), generator=gen, device=dev, dtype=torch.int8)
+    s_rel = (torch.rand(n, k // 16, generator=gen, device=dev) * 180 + 20).to(torch.float8_e4m3fn)
+    s_ch = torch.rand(n, generator=gen, device=dev) * 0.02 + 0.005
+    return W4A8Weight(q, s_rel, s_ch, torch.linspace(-1.0, 1.0, 16, device=dev), group_size=16, convrot=256)
+
+
+@torch.no_grad()
 def synthetic_activation(m: int, k: int, *, outlier_frac: float = 0.005, n_outliers: Optional[int] = None, seed: int = 0,
                          dtype: torch.dtype = torch.bfloat16, device="cuda") -> torch.Tensor:
     dev = torch.device(device)
