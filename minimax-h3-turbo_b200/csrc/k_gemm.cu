@@ -4,6 +4,19 @@
 
 namespace h3b {
 
+// Bytes of weight rows one super-column of output tiles may span (the CTAs working at the same time read them all, so
+// they should stay in L2 while the activation rows stream past).  H3B_GEMM_GN_MB in the environment overrides the
+// default (read once per process; for sweeps).
+static int64_t gn_budget() {
+  static int64_t v = -1;
+  if (v < 0) {
+    const char* e = getenv("H3B_GEMM_GN_MB");
+    const long mb = e ? atol(e) : 0;
+    v = (mb > 0 ? mb : 24) << 20;
+  }
+  return v;
+}
+
 template <int BN, int OUT, bool BIAS, int QMODE>
 static int launch_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, const float* xs, const float* sch,
                        const void* bias, void* out, int64_t ldo, int M, int N, int K, cudaStream_t st) {
@@ -26,9 +39,9 @@ static int launch_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int sms = num_sms();
   const int grid = tiles < sms ? tiles : sms;
-  // weight block per super-column <= ~24 MB of int8 rows, so it stays in L2 while every M tile passes over it
+  // weight block per super-column <= gn_budget() bytes of int8 rows, so it stays in L2 while every M tile passes over it
   const int n_tiles = (N + BN - 1) / BN;
-  int gn = static_cast<int>((24ll << 20) / (static_cast<int64_t>(BN) * K));
+  int gn = static_cast<int>(gn_budget() / (static_cast<int64_t>(BN) * K));
   gn = gn < 1 ? 1 : (gn > n_tiles ? n_tiles : gn);
   kern<<<grid, 192, C::SMEM, st>>>(ta, tb, xs, sch, bias, out, ldo, M, N, K, gn);
   return check_launch("gemm_i8_kernel");
@@ -74,7 +87,7 @@ static int launch_gemm_pair(const int8_t* a, int64_t lda, const int8_t* b, int64
   const int tiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
   const int pairs = tiles < max_pairs[dev & 63] ? tiles : max_pairs[dev & 63];
   const int n_tiles = (N + P_BN - 1) / P_BN;
-  int gn = static_cast<int>((24ll << 20) / (static_cast<int64_t>(P_BN) * K));
+  int gn = static_cast<int>(gn_budget() / (static_cast<int64_t>(P_BN) * K));
   gn = gn < 1 ? 1 : (gn > n_tiles ? n_tiles : gn);
   kern<<<2 * pairs, 192, P_SMEM, st>>>(ta, tb, xs, sch, bias, out, ldo, M, N, K, gn);
   return check_launch("gemm_i8_pair_kernel");

@@ -407,9 +407,11 @@ __global__ void __launch_bounds__(SPLIT ? 512 : 1024) rotq_kernel(const void* __
           mA = fmaxf(mA, fabsf(y));
         }
       } else if constexpr (DT == DT_BF16 && MODE == MODE_CK) {
-        if constexpr (RG == 1) {  // split: both lanes are the same row
+        if constexpr (RG == 1) {  // split: both lanes are the same row; four independent chains
+          float m4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int i = 0; i < 16; ++i) mA = max3f(mA, fabsf(v[i].x), fabsf(v[i].y));
+          for (int i = 0; i < 16; ++i) m4[i & 3] = max3f(m4[i & 3], fabsf(v[i].x), fabsf(v[i].y));
+          mA = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
         } else {
 #pragma unroll
           for (int i = 0; i < 16; i += 2) {
@@ -554,14 +556,19 @@ __host__ __device__ constexpr int rowk_xbytes() { return 2 * xgrp(16) * 8; }  //
 // transform's column writes (16 threads, element t + 16 i) and the quantiser's row reads (thread t', 16-byte chunks of
 // row t') are both free of bank conflicts.
 constexpr int ROWK_BLOCK_WORDS = 16 * 16 + 16;
+constexpr int ROWK_PASS_BYTES = 2 * ROWK_BLOCK_WORDS * 4;  // a pass's part of the row buffer (two blocks)
 // A thread's two lanes are the same row, `rowk_off(K)` elements apart: K / 2 when K is a multiple of 512, otherwise
 // (K a multiple of 256 only, e.g. the official width 5376 = 21 x 256) half a ConvRot block more, so that both lanes sit
 // at the same position of their blocks; the upper lane then runs off the end of the row for the last 128 elements of
 // the lower half, where it loads zeros (no effect on the transform of other blocks or on the absmax) and stores nothing.
 __host__ __device__ constexpr int64_t rowk_off(int64_t K) { return (K + 511) / 512 * 256; }
 __host__ __device__ constexpr int rowk_passes(int64_t K) { return static_cast<int>((2 * rowk_off(K) + ROWK_PASS - 1) / ROWK_PASS); }
+// A warp's shared memory: the row buffer, then a tail.  Pass p's exchange area starts where the pass's part of the row
+// buffer starts: that part and those of the later passes hold nothing yet (the pass writes its part only after the
+// exchange is read back), so only the last pass's exchange reaches past the row buffer, into the tail.
 __host__ __device__ inline size_t rowk_warp_bytes(int64_t K) {
-  return static_cast<size_t>(rowk_passes(K)) * (2 * ROWK_BLOCK_WORDS * 4) + rowk_xbytes();
+  return static_cast<size_t>(rowk_passes(K)) * ROWK_PASS_BYTES +
+         (rowk_xbytes() > ROWK_PASS_BYTES ? rowk_xbytes() - ROWK_PASS_BYTES : 0);
 }
 __device__ __forceinline__ int rowk_word(int i, int col) { return 16 * i + 4 * ((col >> 2) ^ ((i >> 1) & 3)) + (col & 3); }
 
@@ -599,9 +606,10 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
                                                    // upper half-warp idles
   unsigned char* wbase = rotq_smem + static_cast<size_t>(warp) * rowk_warp_bytes(K);
   const int t = lane & 15;
-  // this half-warp's block in the row buffer of pass 0 (passes are 2 blocks apart)
-  uint32_t* bblk = reinterpret_cast<uint32_t*>(wbase + rowk_xbytes()) + (lane >> 4) * ROWK_BLOCK_WORDS;
-  float2* gbuf = reinterpret_cast<float2*>(wbase) + (lane >> 4) * xgrp(16);
+  // this half-warp's block in the row buffer of pass 0 (passes are 2 blocks apart), and its exchange area in pass 0
+  // (the exchange of pass p sits ROWK_PASS_BYTES * p further on)
+  uint32_t* bblk = reinterpret_cast<uint32_t*>(wbase) + (lane >> 4) * ROWK_BLOCK_WORDS;
+  float2* gbuf0 = reinterpret_cast<float2*>(wbase) + (lane >> 4) * xgrp(16);
   const int64_t rstep = static_cast<int64_t>(gridDim.x) * nw;
   int64_t row = static_cast<int64_t>(blockIdx.x) * nw + warp;
 
@@ -712,6 +720,7 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
 #pragma unroll
       for (int d = 0; d < 4; ++d) h4(v[d], v[d + 4], v[d + 8], v[d + 12], 1.0f);
       {
+        float2* gbuf = gbuf0 + p * (ROWK_PASS_BYTES / 8);
         float4* wr = reinterpret_cast<float4*>(gbuf + t * XROW);
 #pragma unroll
         for (int i = 0; i < 8; ++i) wr[i] = make_float4(v[2 * i].x, v[2 * i].y, v[2 * i + 1].x, v[2 * i + 1].y);
@@ -729,17 +738,18 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
       uint32_t bw[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) bw[i] = pack2<DT>(v[i]);
-      float mP = 0.f;
+      float m4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
       if constexpr (MODE == MODE_CK) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) mP = max3f(mP, fabsf(v[i].x), fabsf(v[i].y));
+        for (int i = 0; i < 16; ++i) m4[i & 3] = max3f(m4[i & 3], fabsf(v[i].x), fabsf(v[i].y));
       } else {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 b = unpack2<DT>(bw[i]);
-          mP = max3f(mP, fabsf(b.x), fabsf(b.y));
+          m4[i & 3] = max3f(m4[i & 3], fabsf(b.x), fabsf(b.y));
         }
       }
+      const float mP = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
       if (32 * p + lane < nchunk) mA = fmaxf(mA, mP);
       uint32_t* bp = bblk + p * (2 * ROWK_BLOCK_WORDS);
 #pragma unroll
@@ -782,6 +792,7 @@ __global__ void __launch_bounds__(256) rotq_row_kernel(const void* __restrict__ 
         if (half + 16ll * c < K) *reinterpret_cast<uint4*>(qrow + half + 16ll * c) = make_uint4(wB[0], wB[1], wB[2], wB[3]);
       }
     }
+    __syncwarp();  // the next row's first exchange overwrites row buffer parts that the loop above read
   }
 }
 
