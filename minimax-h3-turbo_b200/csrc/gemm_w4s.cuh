@@ -11,12 +11,14 @@
 //   warps 7..   decoders: a P stage -> the BN x 128 int8 B tile of an AB stage (level tables + byte permutes, exactly
 //               decode.cuh's levels, 128-byte swizzle), then fence.proxy.async and an arrival per warp
 //   warp 1      MMA issuer: per k-block and M subtile 4 x tcgen05.mma.kind::i8 (K = 32 each) into its TMEM accumulator
-//   warps 2-5   epilogue: with one split, tcgen05.ld -> the W4A8 epilogue (as gemm_sm100.cuh) -> the output; with
-//               several, the raw int32 partial sums -> part[s][m][n] in the caller's workspace, and a second kernel
-//               (w4s_reduce_kernel, launched as a programmatic dependent so its launch overlaps this grid's tail) adds
-//               the splits in a fixed order and applies the epilogue.
+//   warps 2-5   epilogue: with one split, tcgen05.ld -> the W4A8 epilogue (as gemm_sm100.cuh) -> the output.  With S
+//               splits, the S CTAs of one output tile form a thread-block cluster: each stages its raw int32 partial
+//               sums in its own (by then idle) ring memory, and after a cluster barrier every CTA of the cluster adds
+//               up 1/S of the tile's rows over the S CTAs' staging areas in rank order (distributed shared memory
+//               loads), applies the epilogue and stores the output -- no partial sums in HBM, no second kernel.
 // The P ring is separate from (and deeper than) the AB ring, so weight bytes keep streaming from HBM while the tensor
-// core works on earlier k-blocks.  One work unit per CTA; every wait bounded (h3b_common.cuh).
+// core works on earlier k-blocks.  One work unit per CTA; every mbarrier wait bounded (h3b_common.cuh), and every CTA
+// reaches both cluster barriers of each subtile whatever happened before, so no CTA waits for a peer that left.
 #pragma once
 
 #include "decode.cuh"
@@ -34,7 +36,6 @@ struct W4sEpi {
   int64_t ldo;
   int out_dtype;       // H3B_BF16 / H3B_FP16 / H3B_FP32 / H3B_INT32
   int qmode;           // H3B_QMODE_CK / H3B_QMODE_EAGER
-  int32_t* part;       // [splits][M][N] partial sums (splits > 1), else null
 };
 
 template <int BN, int MS>
@@ -60,12 +61,20 @@ struct W4sCfg {
   static constexpr int SMEM = 1024 + A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES + 4096 + 512;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
   static_assert(P_STAGES >= 2 && CPT * 32 * DWARPS == BN * 8 && 8 % CPT == 0, "bad small-M GEMM configuration");
-  static_assert(A_STAGES * MS * A_BYTES >= 4 * 32 * 33 * 4, "the epilogue's transpose squares live in the activation ring");
+  // the split-K staging of one 128-row subtile: [128][BN + 4] int32 (rows 16 bytes apart in bank terms), in the rings
+  static constexpr int RED_STRIDE = BN + 4;
+  static_assert(BM * RED_STRIDE * 4 <= A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES,
+                "the split-K staging lives in the ring memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// 16 bytes of another cluster CTA's shared memory (`addr`: a shared::cluster address)
+__device__ __forceinline__ uint4 ld_cluster_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
 
 // The W4A8 epilogue of `n` (<= 8) consecutive accumulators of one row, runtime dtype / mode (the same operations, in the
 // same order, as epilogue_row32: (fp32(acc) * xs) * s_ch or fp32(acc) * (xs * s_ch), rounded to the output dtype, then
@@ -163,8 +172,9 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = (N + BN - 1) / BN;
-  // unit = (split, M tile, N tile), N fastest: the CTAs of one split and M tile run together and share activation rows
-  const int nt = blockIdx.x % n_tiles, mt = (blockIdx.x / n_tiles) % m_tiles, split = blockIdx.x / (n_tiles * m_tiles);
+  // unit = (M tile, N tile, split), split fastest: the S splits of one output tile are one cluster, split = cluster rank
+  const int split = blockIdx.x % splits, tile = blockIdx.x / splits;
+  const int nt = tile % n_tiles, mt = tile / n_tiles;
   const int row_base = mt * MS * BM;  // first activation / output row of this CTA
   const int num_kb = (K + BK - 1) / BK;
   const int kb0 = static_cast<int>(static_cast<int64_t>(split) * num_kb / splits);
@@ -200,7 +210,6 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmP);
-    pdl_launch_dependents();  // the reduction kernel may be scheduled now; it waits for this grid to finish
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -274,32 +283,7 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
     const bool ok = mbar_wait(tfull, 0, abort_flag);
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
-      if (splits > 1) {
-        // raw int32 partial sums of this split -> part[split][m][n], coalesced: each warp's 32 rows x 32 columns go
-        // through a padded shared-memory square (the activation ring is free: every MMA has completed), and every
-        // store instruction then writes 32 consecutive columns of one row
-        int32_t* sq = reinterpret_cast<int32_t*>(sA) + quad * (32 * 33);
-        int32_t* pbase = epi.part + static_cast<int64_t>(split) * M * N;
-#pragma unroll 1
-        for (int ms = 0; ms < MS; ++ms) {
-          const int row0 = row_base + ms * BM + quad * 32;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ms * BN + c * 32), r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) sq[lane * 33 + j] = static_cast<int32_t>(r[j]);
-            __syncwarp();
-            const int64_t n = static_cast<int64_t>(nt) * BN + c * 32 + lane;
-            for (int rr = 0; rr < 32; ++rr) {
-              const int row = row0 + rr;
-              if (row < M && n < N) pbase[static_cast<int64_t>(row) * N + n] = sq[rr * 33 + lane];
-            }
-            __syncwarp();
-          }
-        }
-      } else {
+      if (splits == 1) {
         const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
         const bool vec_ok = (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
 #pragma unroll 1
@@ -397,53 +381,77 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (splits > 1) {  // ------------------------------------------------------------- split-K reduction in the cluster
+    tc_fence_after();
+    int32_t* red = reinterpret_cast<int32_t*>(sA);  // every ring is idle now: all MMAs and copies have completed
+    const uint32_t red_u32 = smem_u32(red);
+    const uint32_t rank = static_cast<uint32_t>(split);
+    const int r0 = BM * split / splits, r1 = BM * (split + 1) / splits;  // this CTA's rows of each subtile
+    constexpr int VPR = BN / 8;
+    const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
+    const bool vec_ok = (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
+    const bool ok = *abort_flag == 0;
+#pragma unroll 1
+    for (int ms = 0; ms < MS; ++ms) {
+      if (warp >= 2 && warp < 6) {  // stage: TMEM lane (quad * 32 + lane) = subtile row, 32 columns per load
+        const int quad = warp & 3;
+        int32_t* rrow = red + (quad * 32 + lane) * C::RED_STRIDE;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ms * BN + c * 32), r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            reinterpret_cast<uint4*>(rrow + c * 32)[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+        }
+      }
+      cluster_sync();  // every CTA of the tile has staged subtile ms
+      if (ok) {
+        for (int it = threadIdx.x; it < (r1 - r0) * VPR; it += blockDim.x) {
+          const int rl = r0 + it / VPR, g = it - (it / VPR) * VPR;
+          const int row = row_base + ms * BM + rl;
+          const int64_t n0 = static_cast<int64_t>(nt) * BN + 8 * g;
+          if (row >= M || n0 >= N) continue;
+          const uint32_t off = red_u32 + static_cast<uint32_t>((rl * C::RED_STRIDE + 8 * g) * 4);
+          int32_t a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          for (int p = 0; p < splits; ++p) {  // rank order, the same sum on every run
+            const uint32_t src = p == static_cast<int>(rank) ? off : mapa_rank(off, static_cast<uint32_t>(p));
+            const uint4 x = ld_cluster_v4(src), y = ld_cluster_v4(src + 16);
+            a[0] += static_cast<int32_t>(x.x); a[1] += static_cast<int32_t>(x.y);
+            a[2] += static_cast<int32_t>(x.z); a[3] += static_cast<int32_t>(x.w);
+            a[4] += static_cast<int32_t>(y.x); a[5] += static_cast<int32_t>(y.y);
+            a[6] += static_cast<int32_t>(y.z); a[7] += static_cast<int32_t>(y.w);
+          }
+          const int nn = N - n0 < 8 ? static_cast<int>(N - n0) : 8;
+          const float xsr = epi.out_dtype == H3B_INT32 ? 0.f : epi.xs[row];
+          char* orow = static_cast<char*>(epi.out) + static_cast<size_t>(row) * static_cast<size_t>(epi.ldo) * osz;
+          w4s_store8(a, nn, xsr, epi, orow, n0, vec_ok && nn == 8);
+        }
+      }
+      cluster_sync();  // the peers have read this CTA's staging before it is overwritten or the CTA exits
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
-// Sum of the splits' int32 partial sums, in split order, then the W4A8 epilogue; one thread per 8 output columns.
-// Launched as a programmatic dependent of gemm_w4s_kernel: it waits for that grid (and its memory) before reading.
-static __global__ void __launch_bounds__(256) w4s_reduce_kernel(const W4sEpi epi, int M, int N, int splits) {
-  pdl_wait_primary();
-  const int vpr = (N + 7) / 8;
-  const int64_t total = static_cast<int64_t>(M) * vpr;
-  const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
-  const bool vec_ok = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(epi.part) & 15) == 0 &&
-                      (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
-       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int row = static_cast<int>(v / vpr);
-    const int64_t n0 = (v - static_cast<int64_t>(row) * vpr) * 8;
-    const int nn = N - n0 < 8 ? static_cast<int>(N - n0) : 8;
-    int32_t a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int s = 0; s < splits; ++s) {
-      const int32_t* p = epi.part + (static_cast<int64_t>(s) * M + row) * N + n0;
-      if (vec_ok && nn == 8) {
-        const int4 x = __ldcs(reinterpret_cast<const int4*>(p)), y = __ldcs(reinterpret_cast<const int4*>(p) + 1);
-        a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w; a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (j < nn) a[j] += p[j];
-      }
-    }
-    const float xsr = epi.out_dtype == H3B_INT32 ? 0.f : epi.xs[row];
-    char* orow = static_cast<char*>(epi.out) + static_cast<size_t>(row) * static_cast<size_t>(epi.ldo) * osz;
-    w4s_store8(a, nn, xsr, epi, orow, n0, vec_ok && nn == 8);
-  }
-}
-
 // ------------------------------------------------------------------------------------------------ host side
-// The work split: all M rows per CTA (MS subtiles), then the N tile width and the number of K splits that give the
-// shortest estimated time -- one wave of at most `sms` CTAs, each doing ceil(num_kb / S) k-blocks of MS x BN x 128 x
-// 128 MACs, plus (S > 1) writing and re-reading S x M x N int32 partial sums through L2 and the reduction's launch.
+// The work split: all M rows per CTA (MS subtiles) or one CTA per 128-row M tile, then the N tile width and the number
+// of K splits S <= 8 (a portable cluster) that give the shortest estimated time -- one wave of at most cap[S] CTAs
+// (clusters of S CTAs that can be resident at once), each doing ceil(num_kb / S) k-blocks, plus the in-cluster
+// reduction.  Clocks per k-block: the decode of a BN x 128 weight tile by the decoder warps (~7.5 per weight row, the
+// usual bound), the tensor core (~3 per output column per subtile), the activation tile through L2 (~64 B/clock), the
+// activation ring covering ~3000 clocks of load latency.
 struct W4sPlan {
   int bn, ms, splits;  // N tile, 128-row M subtiles per CTA (1: one CTA per M tile), K splits
 };
 
-inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, int sms) {
+inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, const int (&cap)[9]) {
   const int64_t num_kb = (K + BK - 1) / BK;
   W4sPlan best{128, M <= BM ? 1 : 2, 1};
   double best_t = -1;
@@ -453,15 +461,15 @@ inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, int sms) {
     for (int bn : {256, 192, 128}) {
       const int64_t n_tiles = (N + bn - 1) / bn;
       const int a_stages = ms == 1 ? 6 : (bn == 128 ? 4 : 3);
-      for (int s = 1; s <= 16 && s <= num_kb; ++s) {
+      for (int s = 1; s <= 8 && s <= num_kb; ++s) {
+        if (cap[s] < s) continue;
         const int64_t units = m_tiles * n_tiles * s;
-        const int64_t waves = (units + sms - 1) / sms;
+        const int64_t waves = (units + cap[s] - 1) / cap[s];
         if (waves > 1 && s > 1) break;
-        // clocks per k-block: the tensor core (ms x bn x 2), the activation tile through L2 (~64 B/clock per SM), and
-        // the activation ring covering ~3000 clocks of load latency
-        const double mma = ms * bn * 2.0, afetch = ms * BM * BK / 64.0, lat = 3000.0 / a_stages;
-        const double t_kb = mma > afetch ? (mma > lat ? mma : lat) : (afetch > lat ? afetch : lat);
-        const double red = s > 1 ? 4000.0 + static_cast<double>(s) * M * N * 4 / 2048.0 : 0.0;
+        const double dec = bn * 7.5, mma = ms * bn * 3.0, afetch = ms * BM * BK / 64.0, lat = 3000.0 / a_stages;
+        double t_kb = dec;
+        for (double c : {mma, afetch, lat}) t_kb = c > t_kb ? c : t_kb;
+        const double red = s > 1 ? ms * (2000.0 + bn * 8.0) : 0.0;
         const double t = static_cast<double>(waves) * ((num_kb + s - 1) / s) * t_kb + 4000.0 + red;
         if (best_t < 0 || t < best_t) {
           best_t = t;
@@ -473,60 +481,103 @@ inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, int sms) {
   return best;
 }
 
-inline size_t w4s_partial_bytes(int64_t M, int64_t N, int splits) {
-  return splits > 1 ? static_cast<size_t>(splits) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4 : 0;
+template <int BN, int MS, int SDT>
+static int w4s_set_attrs() {
+  using C = W4sCfg<BN, MS>;
+  static std::atomic<unsigned long long> attr_done{0};  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_done.load() & bit)) {
+    const cudaError_t e = cudaFuncSetAttribute(gemm_w4s_kernel<BN, MS, SDT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm w4s)");
+    attr_done.fetch_or(bit);
+  }
+  return 0;
+}
+
+// CTAs that can be resident at once for each cluster size 1..8 (every configuration takes one CTA per SM), queried
+// once per device on the 256-column one-subtile kernel.
+template <int SDT>
+static int w4s_capacity(int (&cap)[9]) {
+  static std::mutex mu;
+  static int cached[64][9];
+  static unsigned long long done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!(done & (1ull << (dev & 63)))) {
+    if (int rc = w4s_set_attrs<256, 1, SDT>()) return rc;
+    int* c = cached[dev & 63];
+    c[0] = 0;
+    c[1] = num_sms();
+    for (int s = 2; s <= 8; ++s) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(s), 1, 1);
+      cfg.blockDim = dim3(W4sCfg<256, 1>::THREADS, 1, 1);
+      cfg.dynamicSmemBytes = W4sCfg<256, 1>::SMEM;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = static_cast<unsigned>(s);
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_w4s_kernel<256, 1, SDT>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+      c[s] = n * s;
+    }
+    done |= 1ull << (dev & 63);
+  }
+  for (int s = 0; s < 9; ++s) cap[s] = cached[dev & 63][s];
+  return 0;
 }
 
 template <int BN, int MS, int SDT>
 static int w4s_launch_cfg(int splits, const CUtensorMap& ta, const CUtensorMap& tp, const void* s_rel, int64_t lds,
                           const float* codebook, const W4sEpi& epi, int M, int N, int K, cudaStream_t st) {
   using C = W4sCfg<BN, MS>;
-  auto kern = gemm_w4s_kernel<BN, MS, SDT>;
-  static std::atomic<unsigned long long> attr_done{0};  // one bit per device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(attr_done.load() & bit)) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm w4s)");
-    attr_done.fetch_or(bit);
-  }
+  if (int rc = w4s_set_attrs<BN, MS, SDT>()) return rc;
   const int m_tiles = MS == 1 ? (M + BM - 1) / BM : 1;
   const int units = ((N + BN - 1) / BN) * m_tiles * splits;
-  kern<<<units, C::THREADS, C::SMEM, st>>>(ta, tp, s_rel, lds, codebook, epi, M, N, K, splits, m_tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(units), 1, 1);
+  cfg.blockDim = dim3(C::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;  // the splits of one output tile are one cluster
+  attr.val.clusterDim.x = static_cast<unsigned>(splits);
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_w4s_kernel<BN, MS, SDT>, ta, tp, s_rel, lds, codebook, epi, M, N, K,
+                                           splits, m_tiles);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemm_w4s_kernel)");
   return check_launch("gemm_w4s_kernel");
 }
 
-// The small-M GEMM of one scale dtype: the main kernel, then (splits > 1) the reduction as a programmatic dependent.
+// The small-M GEMM of one scale dtype: plan (or `force`, when not null), then one clustered launch.
 template <int SDT>
-int w4s_launch_sdt(const W4sPlan& plan, const int8_t* a, int64_t lda, const void* q4, int64_t ldq4, const void* s_rel,
+int w4s_launch_sdt(const W4sPlan* force, const int8_t* a, int64_t lda, const void* q4, int64_t ldq4, const void* s_rel,
                    int64_t lds, const float* codebook, const W4sEpi& epi, int M, int N, int K, cudaStream_t st) {
+  int cap[9];
+  if (int rc = w4s_capacity<SDT>(cap)) return rc;
+  const W4sPlan plan = force ? *force : w4s_plan(M, N, K, cap);
+  if (plan.splits < 1 || plan.splits > 8) return fail(H3B_ERR_ARG, "small-M GEMM: 1 to 8 K splits");
   CUtensorMap ta, tp;
   int rc = make_map(&ta, a, K, M, lda, BM);
   if (rc) return rc;
   rc = make_map_packed(&tp, q4, K / 2, N, ldq4, plan.bn);
   if (rc) return rc;
-#define H3B_W4S(B, S) if (plan.bn == B && plan.ms == S) rc = w4s_launch_cfg<B, S, SDT>(plan.splits, ta, tp, s_rel, lds, codebook, epi, M, N, K, st); else
+#define H3B_W4S(B, S) if (plan.bn == B && plan.ms == S) return w4s_launch_cfg<B, S, SDT>(plan.splits, ta, tp, s_rel, lds, codebook, epi, M, N, K, st);
   H3B_W4S(256, 2) H3B_W4S(192, 2) H3B_W4S(128, 2) H3B_W4S(256, 1) H3B_W4S(192, 1) H3B_W4S(128, 1)
-  return fail(H3B_ERR_ARG, "small-M GEMM: unsupported tile plan");
 #undef H3B_W4S
-  if (rc || plan.splits == 1) return rc;
-  cudaLaunchConfig_t cfg = {};
-  int sms = num_sms();
-  const int64_t vecs = static_cast<int64_t>(M) * ((N + 7) / 8);
-  const int64_t want = (vecs + 255) / 256;
-  cfg.gridDim = dim3(static_cast<unsigned>(want < 4ll * sms ? want : 4ll * sms), 1, 1);
-  cfg.blockDim = dim3(256, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr.val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, w4s_reduce_kernel, epi, M, N, plan.splits);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(w4s_reduce_kernel)");
-  return check_launch("w4s_reduce_kernel");
+  return fail(H3B_ERR_ARG, "small-M GEMM: unsupported tile plan");
 }
 
 }  // namespace h3b

@@ -23,13 +23,13 @@ extern template int w4_launch_sdt<H3B_FP32>(int, int, int, const int8_t*, int64_
                                             int64_t, const float*, const float*, const float*, const void*, void*,
                                             int64_t, int, int, int, cudaStream_t);
 
-extern template int w4s_launch_sdt<H3B_FP8_E4M3>(const W4sPlan&, const int8_t*, int64_t, const void*, int64_t, const void*,
+extern template int w4s_launch_sdt<H3B_FP8_E4M3>(const W4sPlan*, const int8_t*, int64_t, const void*, int64_t, const void*,
                                                  int64_t, const float*, const W4sEpi&, int, int, int, cudaStream_t);
-extern template int w4s_launch_sdt<H3B_FP16>(const W4sPlan&, const int8_t*, int64_t, const void*, int64_t, const void*,
+extern template int w4s_launch_sdt<H3B_FP16>(const W4sPlan*, const int8_t*, int64_t, const void*, int64_t, const void*,
                                              int64_t, const float*, const W4sEpi&, int, int, int, cudaStream_t);
-extern template int w4s_launch_sdt<H3B_BF16>(const W4sPlan&, const int8_t*, int64_t, const void*, int64_t, const void*,
+extern template int w4s_launch_sdt<H3B_BF16>(const W4sPlan*, const int8_t*, int64_t, const void*, int64_t, const void*,
                                              int64_t, const float*, const W4sEpi&, int, int, int, cudaStream_t);
-extern template int w4s_launch_sdt<H3B_FP32>(const W4sPlan&, const int8_t*, int64_t, const void*, int64_t, const void*,
+extern template int w4s_launch_sdt<H3B_FP32>(const W4sPlan*, const int8_t*, int64_t, const void*, int64_t, const void*,
                                              int64_t, const float*, const W4sEpi&, int, int, int, cudaStream_t);
 
 // The small-M split-K kernel serves M <= 256 (H3B_W4S=0 in the environment turns it off: read once per process; for
@@ -54,32 +54,24 @@ bool w4_fused_ok(int64_t M, int64_t N, int64_t K, const void* q4, int64_t ldq4, 
   return bn <= 192 && M <= 1024;
 }
 
-size_t w4_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  if (!w4s_enabled(M) || N <= 0 || K <= 0) return 0;
-  const W4sPlan plan = w4s_plan(M, N, K, num_sms());
-  return w4s_partial_bytes(M, N, plan.splits);
-}
-
 int gemm_w4_launch(const int8_t* a, int64_t lda, const void* q4, int64_t ldq4, const void* s_rel, int s_dtype,
                    int64_t lds, const float* codebook, const float* xs, const float* sch, const void* bias, void* out,
-                   int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, int qmode, void* ws, size_t ws_bytes,
-                   cudaStream_t st) {
+                   int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, int qmode, cudaStream_t st) {
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   if (w4s_enabled(M)) {
-    W4sPlan plan = w4s_plan(M, N, K, num_sms());
     // H3B_W4S_PLAN="bn,splits,subtiles" in the environment replaces the planner's choice (read per call; for tile
     // sweeps)
+    W4sPlan forced{0, 0, 0};
+    const W4sPlan* plan = nullptr;
     if (const char* e = getenv("H3B_W4S_PLAN")) {
       int bn = 0, sp = 0, ms = 0;
-      if (sscanf(e, "%d,%d,%d", &bn, &sp, &ms) == 3 && (bn == 128 || bn == 192 || bn == 256) && sp >= 1 &&
-          sp <= static_cast<int>((K + BK - 1) / BK) && (ms == 1 || (ms == 2 && M <= 2 * BM)))
-        plan = W4sPlan{bn, ms, sp};
+      if (sscanf(e, "%d,%d,%d", &bn, &sp, &ms) == 3 && (bn == 128 || bn == 192 || bn == 256) && sp >= 1 && sp <= 8 &&
+          sp <= static_cast<int>((K + BK - 1) / BK) && (ms == 1 || (ms == 2 && M <= 2 * BM))) {
+        forced = W4sPlan{bn, ms, sp};
+        plan = &forced;
+      }
     }
-    // fewer splits when the caller's workspace cannot hold the partial sums (int32 [splits, M, N], 16-byte aligned)
-    const size_t per_split = static_cast<size_t>(M) * static_cast<size_t>(N) * 4;
-    if (plan.splits > 1 && (!ws || (reinterpret_cast<uintptr_t>(ws) & 15))) plan.splits = 1;
-    while (plan.splits > 1 && static_cast<size_t>(plan.splits) * per_split > ws_bytes) --plan.splits;
-    const W4sEpi epi{xs, sch, bias, out, ldo, out_dtype, qmode, plan.splits > 1 ? static_cast<int32_t*>(ws) : nullptr};
+    const W4sEpi epi{xs, sch, bias, out, ldo, out_dtype, qmode};
     switch (s_dtype) {
       case H3B_FP8_E4M3: return w4s_launch_sdt<H3B_FP8_E4M3>(plan, a, lda, q4, ldq4, s_rel, lds, codebook, epi, m, n, k, st);
       case H3B_FP16: return w4s_launch_sdt<H3B_FP16>(plan, a, lda, q4, ldq4, s_rel, lds, codebook, epi, m, n, k, st);

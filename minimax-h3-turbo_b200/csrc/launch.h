@@ -72,13 +72,10 @@ int gemm_launch(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, cons
 
 // ---- k_w4.cu
 bool w4_fused_ok(int64_t M, int64_t N, int64_t K, const void* q4, int64_t ldq4, int s_dtype, int group);
-// Scratch bytes the decode-in-producer GEMM needs for this problem (split-K partial sums and tile counters; 0 when it
-// runs without a split).
-size_t w4_workspace_bytes(int64_t M, int64_t N, int64_t K);
+// The decode-in-producer GEMM; it needs no scratch (the small-M kernel reduces its K splits inside a cluster).
 int gemm_w4_launch(const int8_t* a, int64_t lda, const void* q4, int64_t ldq4, const void* s_rel, int s_dtype,
                    int64_t lds, const float* codebook, const float* xs, const float* sch, const void* bias, void* out,
-                   int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, int qmode, void* ws, size_t ws_bytes,
-                   cudaStream_t st);
+                   int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, int qmode, cudaStream_t st);
 
 // ---- device failure flags: every translation unit has its own copy of the flag (h3b_common.cuh); each returns its
 // value (after synchronising nothing: the caller synchronises first) and clears it when asked.  0 or a CUDA error.

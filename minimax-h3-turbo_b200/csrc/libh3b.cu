@@ -283,9 +283,8 @@ int h3b_int8_gemm_s32(const int8_t* a, int64_t lda, int64_t M, const int8_t* b, 
 }
 
 size_t h3b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  const size_t grid = static_cast<size_t>(N) * static_cast<size_t>(K);  // the decoded int8 grid (separate decode pass)
-  const size_t part = w4_workspace_bytes(M, N, K);                      // split-K partial sums (small-M kernel)
-  return round_up(grid > part ? grid : part, 256);
+  (void)M;
+  return round_up(static_cast<size_t>(N) * static_cast<size_t>(K), 256);  // the decoded int8 grid (separate decode pass)
 }
 
 size_t h3b_linear_workspace_bytes(int64_t M, int64_t N, int64_t K) {
@@ -314,7 +313,7 @@ int h3b_w4a8_gemm(const int8_t* qa, int64_t lda, const float* xs, int64_t M, con
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (w4_fused_ok(M, N, K, q4, ldq4, s_dtype, group))  // few M tiles: decode inside the GEMM's producer warps
     return gemm_w4_launch(qa, lda, q4, ldq4, s_rel, s_dtype, lds, codebook, xs, s_ch, bias, out, out_dtype, ldo, M, N, K,
-                          quant_mode, workspace, ws_bytes, st);
+                          quant_mode, st);
   int8_t* grid = static_cast<int8_t*>(workspace);
   rc = decode_launch(q4, N, K, ldq4, s_rel, s_dtype, lds, codebook, group, grid, K, st);
   if (rc) return rc;

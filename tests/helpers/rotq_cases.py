@@ -1,5 +1,5 @@
 """Runs the quantiser cases of tests/test_rotq_row_gpu.py in this process and saves codes and scales (torch.save) to
-argv[1].  The test starts it with H3B_ROTQ_ROW=0, so this process uses the CTA-per-row-group kernel for every shape."""
+argv[1].  The test starts it with H3B_ROTQ_ROW=0, so that process uses the CTA-per-row-group kernel for every shape."""
 import sys
 from pathlib import Path
 
@@ -10,7 +10,7 @@ import torch  # noqa: E402
 from minimax_h3_turbo_b200.h3 import qlinear as ql  # noqa: E402
 
 DEV = torch.device("cuda")
-CASES = [  # (M, K, quant mode, SwiGLU input): bf16, ConvRot 256, M >= 4096, K <= 5120 a multiple of 256 (the row kernel)
+CASES = [  # (M, K, quant mode, SwiGLU input): bf16, ConvRot 256, M >= 4096, K <= 6144 a multiple of 256 (the row kernel)
     (4096, 5120, "ck", False),
     (4133, 3072, "eager", False),   # M not a multiple of the warps of a CTA
     (4096, 2560, "ck", True),       # the last pass of a row is half a warp
@@ -19,6 +19,8 @@ CASES = [  # (M, K, quant mode, SwiGLU input): bf16, ConvRot 256, M >= 4096, K <
     (4096, 3840, "ck", False),      # K = 15 x 256, not a multiple of 512: the upper lane runs off the row end
     (4133, 1280, "eager", True),    # the same with a SwiGLU input
     (4096, 256, "ck", False),       # one ConvRot block: the upper lane has nothing at all
+    (4096, 5376, "ck", False),      # the official width: six passes, the last one half a warp
+    (4133, 6144, "eager", False),   # the longest row one warp holds
 ]
 
 

@@ -66,8 +66,7 @@ def test_large_m_keeps_the_separate_decode():
 
 
 def _w4a8_gemm(qa, xs, w, bias, out_dtype, mode):
-    """h3b_w4a8_gemm with the workspace h3b_gemm_workspace_bytes asks for (for M <= 256: the int32 partial sums of the
-    K splits the small-M kernel plans)."""
+    """h3b_w4a8_gemm with the workspace h3b_gemm_workspace_bytes asks for."""
     a = ql._WeightArgs(w)
     m, n, k = qa.shape[0], a.n, a.k
     L = _lib.lib()
@@ -94,9 +93,9 @@ def _w4a8_gemm(qa, xs, w, bias, out_dtype, mode):
     (96, 40, 4096, "fp8", torch.float32, False, "ck"),           # N below one tile
 ])
 def test_small_m_split_k_equals_separate_decode(m, n, k, fmt, dt, bias, mode):
-    """The small-M kernel (all M rows per CTA, K split across CTAs, partial sums reduced by a second kernel) against
-    decode + GEMM, bit for bit.  The planner picks one split for some of these shapes (the epilogue then runs in the
-    GEMM kernel) and several for the others."""
+    """The small-M kernel (all M rows per CTA, K split across the CTAs of a cluster, partial sums added up in the
+    cluster's shared memory) against decode + GEMM, bit for bit.  The planner picks one split for some of these shapes
+    (the epilogue then runs straight from the accumulator) and several for the others."""
     w = synthetic_w4a8(n, k, seed=n + k, device=DEV) if fmt == "fp16" else _fp8_weight(n, k, n + k)
     a = ql._WeightArgs(w)
     assert _lib.lib().h3b_w4a8_gemm_decodes_in_kernel(m, n, k, a.q.data_ptr(), a.ldq, a.s_dtype, a.group) == 1
@@ -122,3 +121,21 @@ def test_small_m_worst_case_accumulators_are_exact():
     xs = torch.ones(m, device=DEV)
     got = _w4a8_gemm(qa, xs, w, None, torch.int32, "ck")
     assert int(got.min()) == int(got.max()) == k * 128 * 127
+
+
+@pytest.mark.parametrize("plan", ["256,8,1", "256,2,2", "192,3,2", "128,5,2", "128,7,1", "192,1,2"])
+def test_small_m_every_tile_plan_is_exact(plan, monkeypatch):
+    """Forced tile plans (N tile, K splits = cluster size, M subtiles per CTA) on a ragged problem: two M subtiles, the
+    second almost empty, N not a multiple of any tile, K splits of unequal length -- bit for bit against decode + GEMM."""
+    m, n, k = 131, 1000, 3584
+    w = synthetic_w4a8(n, k, seed=7, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(11)
+    qa = torch.randint(-128, 128, (m, k), generator=g, device=DEV, dtype=torch.int8)
+    xs = torch.rand(m, generator=g, device=DEV) * 0.05 + 1e-3
+    b = torch.randn(n, generator=g, device=DEV)
+    want = _unfused(qa, xs, w, b, torch.bfloat16, "ck")
+    monkeypatch.setenv("H3B_W4S_PLAN", plan)
+    got = _w4a8_gemm(qa, xs, w, b, torch.bfloat16, "ck")
+    torch.cuda.synchronize()
+    assert torch.equal(got, want), plan
+    assert _lib.lib().h3b_device_error(0) == 0

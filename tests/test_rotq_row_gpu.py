@@ -1,4 +1,4 @@
-"""The warp-per-row rotate+quantise kernel (bf16, ConvRot 256, M >= 4096, K <= 5120 a multiple of 256) against the
+"""The warp-per-row rotate+quantise kernel (bf16, ConvRot 256, M >= 4096, K <= 6144 a multiple of 256) against the
 CTA-per-row-group kernel, bit for bit, and against the oracle: both quantiser modes, SwiGLU inputs, half-warp passes,
 ragged M and degenerate rows (zeros, a value near the bf16 maximum, subnormals only, an infinity)."""
 import os
@@ -19,14 +19,14 @@ def test_row_kernel_equals_the_cta_kernel(tmp_path):
     import rotq_cases
 
     got = rotq_cases.run()
-    ref_file = tmp_path / "cta.pt"
-    env = dict(os.environ, H3B_ROTQ_ROW="0")
-    subprocess.run([sys.executable, str(HERE / "helpers" / "rotq_cases.py"), str(ref_file)], check=True, env=env,
-                   timeout=600)
-    want = torch.load(ref_file)
-    for case, (q, xs), (wq, wxs) in zip(rotq_cases.CASES, got, want):
-        assert torch.equal(q.cpu(), wq), case
-        assert torch.equal(xs.cpu().view(torch.int32), wxs.view(torch.int32)), case
+    for tag, env_add in (("cta", {"H3B_ROTQ_ROW": "0"}),):
+        ref_file = tmp_path / f"{tag}.pt"
+        subprocess.run([sys.executable, str(HERE / "helpers" / "rotq_cases.py"), str(ref_file)], check=True,
+                       env=dict(os.environ, **env_add), timeout=600)
+        want = torch.load(ref_file)
+        for case, (q, xs), (wq, wxs) in zip(rotq_cases.CASES, got, want):
+            assert torch.equal(q.cpu(), wq), (tag, case)
+            assert torch.equal(xs.cpu().view(torch.int32), wxs.view(torch.int32)), (tag, case)
 
 
 def test_row_kernel_against_the_oracle():
@@ -35,7 +35,7 @@ def test_row_kernel_against_the_oracle():
     from oracle import qlinear_oracle as orc
     from minimax_h3_turbo_b200.h3 import qlinear as ql
 
-    for i in (0, 1, 3, 5, 7):  # the cases without SwiGLU (the oracle's exp comes from the host libm)
+    for i in (0, 1, 3, 5, 7, 8, 9):  # the cases without SwiGLU (the oracle's exp comes from the host libm)
         m, k, mode, _ = rotq_cases.CASES[i]
         x = rotq_cases.case_input(i)
         q, xs = ql._quantize_rows(x, 256, mode)
