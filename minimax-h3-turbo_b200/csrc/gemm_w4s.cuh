@@ -12,13 +12,15 @@
 //               decode.cuh's levels, 128-byte swizzle), then fence.proxy.async and an arrival per warp
 //   warp 1      MMA issuer: per k-block and M subtile 4 x tcgen05.mma.kind::i8 (K = 32 each) into its TMEM accumulator
 //   warps 2-5   epilogue: with one split, tcgen05.ld -> the W4A8 epilogue (as gemm_sm100.cuh) -> the output.  With S
-//               splits, the S CTAs of one output tile form a thread-block cluster: each stages its raw int32 partial
-//               sums in its own (by then idle) ring memory, and after a cluster barrier every CTA of the cluster adds
-//               up 1/S of the tile's rows over the S CTAs' staging areas in rank order (distributed shared memory
-//               loads), applies the epilogue and stores the output -- no partial sums in HBM, no second kernel.
+//               splits, the S CTAs of one output tile form a thread-block cluster: CTA p owns 1/S of the tile's rows,
+//               every CTA stores its raw int32 partial sums of each row straight from TMEM into the owner's (by then
+//               idle) ring memory (distributed shared memory stores, posted), and after a cluster barrier each owner
+//               adds up its rows over the S slots in rank order from its own shared memory, applies the epilogue and
+//               stores the output -- no partial sums in HBM, no second kernel, no remote loads.
 // The P ring is separate from (and deeper than) the AB ring, so weight bytes keep streaming from HBM while the tensor
 // core works on earlier k-blocks.  One work unit per CTA; every mbarrier wait bounded (h3b_common.cuh), and every CTA
-// reaches both cluster barriers of each subtile whatever happened before, so no CTA waits for a peer that left.
+// reaches every cluster barrier whatever happened before, so no CTA waits for a peer that left; after the last one no
+// CTA touches another's shared memory.
 #pragma once
 
 #include "decode.cuh"
@@ -61,19 +63,17 @@ struct W4sCfg {
   static constexpr int SMEM = 1024 + A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES + 4096 + 512;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
   static_assert(P_STAGES >= 2 && CPT * 32 * DWARPS == BN * 8 && 8 % CPT == 0, "bad small-M GEMM configuration");
-  // the split-K staging of one 128-row subtile: [128][BN + 4] int32 (rows 16 bytes apart in bank terms), in the rings
+  // the split-K receive area of one 128-row subtile, in the rings: [S][ceil(128 / S)][BN + 4] int32 (rows 16 bytes
+  // apart in bank terms); S ceil(128 / S) <= 128 + 7 rows for S <= 8
   static constexpr int RED_STRIDE = BN + 4;
-  static_assert(BM * RED_STRIDE * 4 <= A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES,
-                "the split-K staging lives in the ring memory");
+  static_assert((BM + 7) * RED_STRIDE * 4 <= A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES,
+                "the split-K receive area lives in the ring memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-// 16 bytes of another cluster CTA's shared memory (`addr`: a shared::cluster address)
-__device__ __forceinline__ uint4 ld_cluster_v4(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
-               : "memory");
-  return v;
+// 16 bytes into a cluster CTA's shared memory (`addr`: a shared::cluster address; a posted store)
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
 // The W4A8 epilogue of `n` (<= 8) consecutive accumulators of one row, runtime dtype / mode (the same operations, in the
@@ -199,11 +199,11 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
     *abort_flag = 0;
     mbar_fence_init();
   }
-  float cb[16];
-  if (warp >= 7) {
+  if constexpr (SDT == H3B_FP8_E4M3) {
+    if (warp >= 7) {
+      float cb[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) cb[i] = __ldg(codebook + i);
-    if constexpr (SDT == H3B_FP8_E4M3) {
+      for (int i = 0; i < 16; ++i) cb[i] = __ldg(codebook + i);
       for (int b = threadIdx.x - 224; b < 256; b += 32 * C::DWARPS) lut[b] = level_table(cb, fp8e4m3_to_f32(static_cast<uint32_t>(b)));
     }
   }
@@ -317,6 +317,25 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
     const int dt = threadIdx.x - 224;             // 0 .. 32 DWARPS - 1
     const int r_loc = (dt * C::CPT) >> 3;         // this thread's row of the B tile
     const int j0 = (dt * C::CPT) & 7;             // its first 16-weight chunk in the row
+    // group-128 scales: the TPR adjacent lanes of one weight row build its level table together, WPT of the four
+    // table words each, and exchange them by shuffles
+    constexpr int TPR = 8 / C::CPT, WPT = 4 / TPR;
+    float cbm[4 * WPT];  // the codebook entries of this lane's table words
+    if constexpr (SDT != H3B_FP8_E4M3) {
+#pragma unroll
+      for (int e = 0; e < 4 * WPT; ++e) cbm[e] = __ldg(codebook + 4 * WPT * (lane % TPR) + e);
+    }
+    auto table = [&](float sc) -> uint4 {
+      uint32_t mine[WPT];
+#pragma unroll
+      for (int w = 0; w < WPT; ++w)
+        mine[w] = pack4(level_of(cbm[4 * w], sc), level_of(cbm[4 * w + 1], sc), level_of(cbm[4 * w + 2], sc),
+                        level_of(cbm[4 * w + 3], sc));
+      uint32_t tw[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) tw[w] = __shfl_sync(0xffffffffu, mine[w % WPT], (lane & ~(TPR - 1)) | (w / WPT));
+      return make_uint4(tw[0], tw[1], tw[2], tw[3]);
+    };
     const int n = nt * BN + r_loc;
     const bool row_ok = n < N;
     const unsigned char* srow = static_cast<const unsigned char*>(s_rel) +
@@ -353,9 +372,11 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
       for (int u = 0; u < C::LA; ++u) {  // unrolled, so the scale ring stays in registers
         const int i = i0 + u;
         if (i >= nkb) break;
-        if (!mbar_wait(&pkfull[ps], pph, abort_flag) || !mbar_wait(&bempty[bs], bph ^ 1u, abort_flag)) { ok = false; break; }
+        // warp-uniform outcome, so that no lane leaves while the others wait in the table's shuffles
+        const bool got = mbar_wait(&pkfull[ps], pph, abort_flag) && mbar_wait(&bempty[bs], bph ^ 1u, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
         uint4 t = make_uint4(0, 0, 0, 0);
-        if constexpr (SDT != H3B_FP8_E4M3) t = level_table(cb, sg[u]);
+        if constexpr (SDT != H3B_FP8_E4M3) t = table(sg[u]);
         const unsigned char* prow = sP + ps * C::P_BYTES + r_loc * (BK / 2);
         unsigned char* brow = sB + bs * C::B_BYTES + r_loc * BK;
 #pragma unroll
@@ -383,9 +404,11 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
   __syncthreads();
   if (splits > 1) {  // ------------------------------------------------------------- split-K reduction in the cluster
     tc_fence_after();
-    int32_t* red = reinterpret_cast<int32_t*>(sA);  // every ring is idle now: all MMAs and copies have completed
+    // receive area [source rank][row - first row of this CTA][column]; every ring is idle now (all MMAs and copies
+    // have completed)
+    int32_t* red = reinterpret_cast<int32_t*>(sA);
     const uint32_t red_u32 = smem_u32(red);
-    const uint32_t rank = static_cast<uint32_t>(split);
+    const int rows_max = (BM + splits - 1) / splits;
     const int r0 = BM * split / splits, r1 = BM * (split + 1) / splits;  // this CTA's rows of each subtile
     constexpr int VPR = BN / 8;
     const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
@@ -393,35 +416,42 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
     const bool ok = *abort_flag == 0;
 #pragma unroll 1
     for (int ms = 0; ms < MS; ++ms) {
-      if (warp >= 2 && warp < 6) {  // stage: TMEM lane (quad * 32 + lane) = subtile row, 32 columns per load
-        const int quad = warp & 3;
-        int32_t* rrow = red + (quad * 32 + lane) * C::RED_STRIDE;
+      // before any push: every CTA of the cluster is done with its rings (they receive the pushes) and, after the first
+      // subtile, has read the previous subtile out of its receive area
+      cluster_sync();
+      if (warp >= 2 && warp < 6) {
+        // push: TMEM lane (quad * 32 + lane) = subtile row r, 32 columns per load, stored straight into the receive
+        // area of the CTA that owns row r, in this CTA's slot (posted stores, no round trip)
+        const int quad = warp & 3, r = quad * 32 + lane;
+        int owner = (r * splits) / BM;  // the owner p has BM p / S <= r < BM (p + 1) / S
+        while (BM * (owner + 1) / splits <= r) ++owner;
+        while (BM * owner / splits > r) --owner;
+        const uint32_t local = red_u32 + static_cast<uint32_t>(((split * rows_max + (r - BM * owner / splits)) * C::RED_STRIDE) * 4);
+        const uint32_t dst = mapa_rank(local, static_cast<uint32_t>(owner));
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ms * BN + c * 32), r);
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ms * BN + c * 32), v);
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            reinterpret_cast<uint4*>(rrow + c * 32)[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            st_cluster_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
       }
-      cluster_sync();  // every CTA of the tile has staged subtile ms
+      cluster_sync();  // every CTA's rows of subtile ms have landed in their owners' receive areas
       if (ok) {
         for (int it = threadIdx.x; it < (r1 - r0) * VPR; it += blockDim.x) {
-          const int rl = r0 + it / VPR, g = it - (it / VPR) * VPR;
-          const int row = row_base + ms * BM + rl;
+          const int rl = it / VPR, g = it - rl * VPR;
+          const int row = row_base + ms * BM + r0 + rl;
           const int64_t n0 = static_cast<int64_t>(nt) * BN + 8 * g;
           if (row >= M || n0 >= N) continue;
-          const uint32_t off = red_u32 + static_cast<uint32_t>((rl * C::RED_STRIDE + 8 * g) * 4);
+          const int32_t* src = red + rl * C::RED_STRIDE + 8 * g;
           int32_t a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
           for (int p = 0; p < splits; ++p) {  // rank order, the same sum on every run
-            const uint32_t src = p == static_cast<int>(rank) ? off : mapa_rank(off, static_cast<uint32_t>(p));
-            const uint4 x = ld_cluster_v4(src), y = ld_cluster_v4(src + 16);
-            a[0] += static_cast<int32_t>(x.x); a[1] += static_cast<int32_t>(x.y);
-            a[2] += static_cast<int32_t>(x.z); a[3] += static_cast<int32_t>(x.w);
-            a[4] += static_cast<int32_t>(y.x); a[5] += static_cast<int32_t>(y.y);
-            a[6] += static_cast<int32_t>(y.z); a[7] += static_cast<int32_t>(y.w);
+            const int4 x = reinterpret_cast<const int4*>(src + p * rows_max * C::RED_STRIDE)[0];
+            const int4 y = reinterpret_cast<const int4*>(src + p * rows_max * C::RED_STRIDE)[1];
+            a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
+            a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
           }
           const int nn = N - n0 < 8 ? static_cast<int>(N - n0) : 8;
           const float xsr = epi.out_dtype == H3B_INT32 ? 0.f : epi.xs[row];
@@ -429,7 +459,6 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
           w4s_store8(a, nn, xsr, epi, orow, n0, vec_ok && nn == 8);
         }
       }
-      cluster_sync();  // the peers have read this CTA's staging before it is overwritten or the CTA exits
     }
   }
   tc_fence_before();
