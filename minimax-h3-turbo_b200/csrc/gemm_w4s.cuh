@@ -71,6 +71,10 @@ struct W4sCfg {
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
+// 16 bytes into this CTA's shared memory (`addr`: a shared::cta address)
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
 // 16 bytes into a cluster CTA's shared memory (`addr`: a shared::cluster address; a posted store)
 __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
@@ -427,15 +431,22 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
         while (BM * (owner + 1) / splits <= r) ++owner;
         while (BM * owner / splits > r) --owner;
         const uint32_t local = red_u32 + static_cast<uint32_t>(((split * rows_max + (r - BM * owner / splits)) * C::RED_STRIDE) * 4);
-        const uint32_t dst = mapa_rank(local, static_cast<uint32_t>(owner));
+        const bool mine = owner == split;  // this CTA's own rows stay on the local path
+        const uint32_t dst = mine ? local : mapa_rank(local, static_cast<uint32_t>(owner));
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ms * BN + c * 32), v);
           tmem_ld_wait();
+          if (mine) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            st_cluster_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            for (int j = 0; j < 8; ++j)
+              st_shared_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              st_cluster_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          }
         }
       }
       cluster_sync();  // every CTA's rows of subtile ms have landed in their owners' receive areas
@@ -471,11 +482,15 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
 
 // ------------------------------------------------------------------------------------------------ host side
 // The work split: all M rows per CTA (MS subtiles) or one CTA per 128-row M tile, then the N tile width and the number
-// of K splits S <= 8 (a portable cluster) that give the shortest estimated time -- one wave of at most cap[S] CTAs
-// (clusters of S CTAs that can be resident at once), each doing ceil(num_kb / S) k-blocks, plus the in-cluster
-// reduction.  Clocks per k-block: the decode of a BN x 128 weight tile by the decoder warps (~7.5 per weight row, the
-// usual bound), the tensor core (~3 per output column per subtile), the activation tile through L2 (~64 B/clock), the
-// activation ring covering ~3000 clocks of load latency.
+// of K splits S <= 4 (larger clusters measured slower: fewer of them fit the GPCs at once) with the shortest estimated
+// time -- one wave of at most cap[S] CTAs (clusters of S CTAs that can be resident at once; several waves only without
+// a split), each doing ceil(num_kb / S) k-blocks.  The terms, in microseconds, were fitted to %globaltimer stamps per CTA
+// phase and graph-timed sweeps of forced plans on B200 (M = 256; (K, N) = (5120, 5120), (5120, 13824), (13824, 5120) and
+// the official fp8 shapes): a k-block costs 0.45 / 0.6 / 0.8 us for one 128-row subtile and BN = 128 / 192 / 256
+// columns, 0.72 / 0.9 / 1.02 us for two (the decode of the weight tile is the bound; two subtiles share it), stretched
+// when fewer than 64 CTAs run; start-up takes 2 us, and each wave ends with either the in-cluster reduction and its
+// epilogue (8.5 us + 0.026 us per subtile column) or, without a split, the four epilogue warps writing the tile alone
+// (0.07 us per subtile column).
 struct W4sPlan {
   int bn, ms, splits;  // N tile, 128-row M subtiles per CTA (1: one CTA per M tile), K splits
 };
@@ -489,17 +504,16 @@ inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, const int (&cap)[9]) {
     const int64_t m_tiles = ms == 1 ? (M + BM - 1) / BM : 1;
     for (int bn : {256, 192, 128}) {
       const int64_t n_tiles = (N + bn - 1) / bn;
-      const int a_stages = ms == 1 ? 6 : (bn == 128 ? 4 : 3);
-      for (int s = 1; s <= 8 && s <= num_kb; ++s) {
+      for (int s = 1; s <= 4 && s <= num_kb; ++s) {
         if (cap[s] < s) continue;
         const int64_t units = m_tiles * n_tiles * s;
         const int64_t waves = (units + cap[s] - 1) / cap[s];
         if (waves > 1 && s > 1) break;
-        const double dec = bn * 7.5, mma = ms * bn * 3.0, afetch = ms * BM * BK / 64.0, lat = 3000.0 / a_stages;
-        double t_kb = dec;
-        for (double c : {mma, afetch, lat}) t_kb = c > t_kb ? c : t_kb;
-        const double red = s > 1 ? ms * (2000.0 + bn * 8.0) : 0.0;
-        const double t = static_cast<double>(waves) * ((num_kb + s - 1) / s) * t_kb + 4000.0 + red;
+        double per_kb = ms == 2 ? (bn == 128 ? 0.72 : bn == 192 ? 0.9 : 1.02) : (bn == 128 ? 0.45 : bn == 192 ? 0.6 : 0.8);
+        if (units < 64) per_kb *= 64.0 / static_cast<double>(units);
+        // every wave pays its k-blocks and its epilogue; start-up once
+        const double epi = s > 1 ? 8.5 + 0.026 * ms * bn : 0.07 * ms * bn;
+        const double t = 2.0 + static_cast<double>(waves) * (((num_kb + s - 1) / s) * per_kb + epi);
         if (best_t < 0 || t < best_t) {
           best_t = t;
           best = W4sPlan{bn, ms, s};
