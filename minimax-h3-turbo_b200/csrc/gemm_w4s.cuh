@@ -11,12 +11,13 @@
 //   warps 7..   decoders: a P stage -> the BN x 128 int8 B tile of an AB stage (level tables + byte permutes, exactly
 //               decode.cuh's levels, 128-byte swizzle), then fence.proxy.async and an arrival per warp
 //   warp 1      MMA issuer: per k-block and M subtile 4 x tcgen05.mma.kind::i8 (K = 32 each) into its TMEM accumulator
-//   warps 2-5   epilogue: with one split, tcgen05.ld -> the W4A8 epilogue (as gemm_sm100.cuh) -> the output.  With S
-//               splits, the S CTAs of one output tile form a thread-block cluster: CTA p owns 1/S of the tile's rows,
-//               every CTA stores its raw int32 partial sums of each row straight from TMEM into the owner's (by then
-//               idle) ring memory (distributed shared memory stores, posted), and after a cluster barrier each owner
-//               adds up its rows over the S slots in rank order from its own shared memory, applies the epilogue and
-//               stores the output -- no partial sums in HBM, no second kernel, no remote loads.
+//   warps 2-5   epilogue: wait for the accumulator, then (with every warp of the CTA, after the roles) stage and store.
+//               The S CTAs of one output tile (S K splits; S = 1 included) form a thread-block cluster: CTA p owns 1/S
+//               of the tile's rows, every CTA stores its raw int32 partial sums of each row straight from TMEM into
+//               the owner's (by then idle) ring memory (distributed shared memory stores, posted; its own rows
+//               locally), and after a cluster barrier each owner adds up its rows over the S slots in rank order from
+//               its own shared memory and all its warps apply the W4A8 epilogue (as gemm_sm100.cuh) and store the
+//               output -- no partial sums in HBM, no second kernel, no remote loads.
 // The P ring is separate from (and deeper than) the AB ring, so weight bytes keep streaming from HBM while the tensor
 // core works on earlier k-blocks.  One work unit per CTA; every mbarrier wait bounded (h3b_common.cuh), and every CTA
 // reaches every cluster barrier whatever happened before, so no CTA waits for a peer that left; after the last one no
@@ -283,40 +284,9 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
       mbar_wait_drain(mdone, 0);
     }
   } else if (warp < 6) {  // ------------------------------------------------------------------- epilogue
-    const int quad = warp & 3;
-    const bool ok = mbar_wait(tfull, 0, abort_flag);
-    if (__all_sync(0xffffffffu, ok)) {
-      tc_fence_after();
-      if (splits == 1) {
-        const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
-        const bool vec_ok = (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
-#pragma unroll 1
-        for (int ms = 0; ms < MS; ++ms) {
-          const int row = row_base + ms * BM + quad * 32 + lane;
-          const float xsr = (epi.out_dtype != H3B_INT32 && row < M) ? epi.xs[row] : 0.f;
-          char* orow = static_cast<char*>(epi.out) + static_cast<size_t>(row) * static_cast<size_t>(epi.ldo) * osz;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ms * BN + c * 32), r);
-            tmem_ld_wait();
-            const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 32;
-            if (row < M && n0 < N) {
-              const int ncols = N - n0 < 32 ? static_cast<int>(N - n0) : 32;
-#pragma unroll
-              for (int g = 0; g < 4; ++g) {
-                const int nn = ncols - 8 * g;
-                if (nn <= 0) break;
-                int32_t a[8];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) a[q] = static_cast<int32_t>(r[8 * g + q]);
-                w4s_store8(a, nn < 8 ? nn : 8, xsr, epi, orow, n0 + 8 * g, vec_ok && nn >= 8);
-              }
-            }
-          }
-        }
-      }
-    }
+    // the accumulator is complete once the last MMA has committed; the epilogue proper runs after the roles, with every
+    // warp of the CTA (below)
+    mbar_wait(tfull, 0, abort_flag);
   } else {  // -------------------------------------------------------------------------------------- decoders
     const int dt = threadIdx.x - 224;             // 0 .. 32 DWARPS - 1
     const int r_loc = (dt * C::CPT) >> 3;         // this thread's row of the B tile
@@ -406,7 +376,7 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (splits > 1) {  // ------------------------------------------------------------- split-K reduction in the cluster
+  {  // -------------------------------------------------------------------- staging, split-K reduction and epilogue
     tc_fence_after();
     // receive area [source rank][row - first row of this CTA][column]; every ring is idle now (all MMAs and copies
     // have completed)
@@ -488,9 +458,9 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
 // phase and graph-timed sweeps of forced plans on B200 (M = 256; (K, N) = (5120, 5120), (5120, 13824), (13824, 5120) and
 // the official fp8 shapes): a k-block costs 0.45 / 0.6 / 0.8 us for one 128-row subtile and BN = 128 / 192 / 256
 // columns, 0.72 / 0.9 / 1.02 us for two (the decode of the weight tile is the bound; two subtiles share it), stretched
-// when fewer than 64 CTAs run; start-up takes 2 us, and each wave ends with either the in-cluster reduction and its
-// epilogue (8.5 us + 0.026 us per subtile column) or, without a split, the four epilogue warps writing the tile alone
-// (0.07 us per subtile column).
+// when fewer than 64 CTAs run; start-up takes 2 us, and each wave ends with the staging and the epilogue: 8.5 us +
+// 0.026 us per subtile column across a cluster, 3 us + 0.055 us per subtile column without a split (measured; the
+// single-CTA epilogue of a whole 128- or 256-row tile is slower per column than a cluster member's share).
 struct W4sPlan {
   int bn, ms, splits;  // N tile, 128-row M subtiles per CTA (1: one CTA per M tile), K splits
 };
@@ -512,7 +482,7 @@ inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, const int (&cap)[9]) {
         double per_kb = ms == 2 ? (bn == 128 ? 0.72 : bn == 192 ? 0.9 : 1.02) : (bn == 128 ? 0.45 : bn == 192 ? 0.6 : 0.8);
         if (units < 64) per_kb *= 64.0 / static_cast<double>(units);
         // every wave pays its k-blocks and its epilogue; start-up once
-        const double epi = s > 1 ? 8.5 + 0.026 * ms * bn : 0.07 * ms * bn;
+        const double epi = s > 1 ? 8.5 + 0.026 * ms * bn : 3.0 + 0.055 * ms * bn;
         const double t = 2.0 + static_cast<double>(waves) * (((num_kb + s - 1) / s) * per_kb + epi);
         if (best_t < 0 || t < best_t) {
           best_t = t;
