@@ -67,8 +67,9 @@ struct W4sCfg {
   // the split-K receive area of one 128-row subtile, in the rings: [S][ceil(128 / S)][BN + 4] int32 (rows 16 bytes
   // apart in bank terms); S ceil(128 / S) <= 128 + 7 rows for S <= 8
   static constexpr int RED_STRIDE = BN + 4;
-  static_assert((BM + 7) * RED_STRIDE * 4 <= A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES,
-                "the split-K receive area lives in the ring memory");
+  static constexpr int RED_WORDS = (BM + 7) * RED_STRIDE;  // one subtile's receive area
+  static constexpr int RING_BYTES = A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES;
+  static_assert(RED_WORDS * 4 <= RING_BYTES, "the split-K receive area lives in the ring memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
@@ -383,15 +384,19 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
     int32_t* red = reinterpret_cast<int32_t*>(sA);
     const uint32_t red_u32 = smem_u32(red);
     const int rows_max = (BM + splits - 1) / splits;
+    // subtiles staged and reduced per round: both at once when their receive areas fit the rings (one pair of cluster
+    // barriers instead of two)
+    const int sub_words = splits * rows_max * C::RED_STRIDE;
+    const int spr = MS * sub_words * 4 <= C::RING_BYTES ? MS : 1;
     const int r0 = BM * split / splits, r1 = BM * (split + 1) / splits;  // this CTA's rows of each subtile
     constexpr int VPR = BN / 8;
     const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
     const bool vec_ok = (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
     const bool ok = *abort_flag == 0;
 #pragma unroll 1
-    for (int ms = 0; ms < MS; ++ms) {
+    for (int m0 = 0; m0 < MS; m0 += spr) {
       // before any push: every CTA of the cluster is done with its rings (they receive the pushes) and, after the first
-      // subtile, has read the previous subtile out of its receive area
+      // round, has read the previous round's subtiles out of its receive area
       cluster_sync();
       if (warp >= 2 && warp < 6) {
         // push: TMEM lane (quad * 32 + lane) = subtile row r, 32 columns per load, stored straight into the receive
@@ -402,31 +407,37 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
         while (BM * owner / splits > r) --owner;
         const uint32_t local = red_u32 + static_cast<uint32_t>(((split * rows_max + (r - BM * owner / splits)) * C::RED_STRIDE) * 4);
         const bool mine = owner == split;  // this CTA's own rows stay on the local path
-        const uint32_t dst = mine ? local : mapa_rank(local, static_cast<uint32_t>(owner));
+        const uint32_t dst0 = mine ? local : mapa_rank(local, static_cast<uint32_t>(owner));
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ms * BN + c * 32), v);
-          tmem_ld_wait();
-          if (mine) {
+        for (int q = 0; q < spr; ++q) {
+          const uint32_t dst = dst0 + static_cast<uint32_t>(q * sub_words * 4);
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>((m0 + q) * BN + c * 32), v);
+            tmem_ld_wait();
+            if (mine) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              st_shared_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          } else {
+              for (int j = 0; j < 8; ++j)
+                st_shared_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              st_cluster_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              for (int j = 0; j < 8; ++j)
+                st_cluster_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
           }
         }
       }
-      cluster_sync();  // every CTA's rows of subtile ms have landed in their owners' receive areas
+      cluster_sync();  // every CTA's rows of this round's subtiles have landed in their owners' receive areas
       if (ok) {
-        for (int it = threadIdx.x; it < (r1 - r0) * VPR; it += blockDim.x) {
-          const int rl = it / VPR, g = it - rl * VPR;
-          const int row = row_base + ms * BM + r0 + rl;
+        const int per_sub = (r1 - r0) * VPR;
+        for (int it = threadIdx.x; it < spr * per_sub; it += blockDim.x) {
+          const int q = it / per_sub, rem = it - q * per_sub;
+          const int rl = rem / VPR, g = rem - rl * VPR;
+          const int row = row_base + (m0 + q) * BM + r0 + rl;
           const int64_t n0 = static_cast<int64_t>(nt) * BN + 8 * g;
           if (row >= M || n0 >= N) continue;
-          const int32_t* src = red + rl * C::RED_STRIDE + 8 * g;
+          const int32_t* src = red + q * sub_words + rl * C::RED_STRIDE + 8 * g;
           int32_t a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
           for (int p = 0; p < splits; ++p) {  // rank order, the same sum on every run
             const int4 x = reinterpret_cast<const int4*>(src + p * rows_max * C::RED_STRIDE)[0];
