@@ -938,6 +938,7 @@ def main():
                          "(overlap), all-gathered first (gather), or passed round a ring")
     ap.add_argument("--no-official", action="store_true", help="sweep line: skip the official-geometry record")
     ap.add_argument("--dit-steps", type=int, default=5, help="sweep line: timed forwards of the config-5 record (config 3: twice as many)")
+    ap.add_argument("--e2e-rows", type=int, default=E2E_ROWS, help="sweep line: tokens per chunk of the end-to-end pipeline")
     ap.add_argument("--no-dit", action="store_true", help="sweep line: skip the config-5 (and, on one GPU, config-3) records")
     args = ap.parse_args()
     args.ms = [int(v) for v in args.ms.split(",") if v]
@@ -1154,10 +1155,11 @@ def run_sweep(args, rank, world, local):
         # so a chunk is an exact sub-problem) over three device input slots, so the upload of chunk j + 1 and the
         # download of chunk j - 1 run while chunk j computes: the host link, not the order of the copies, bounds it
         kmax = max(k for (k, _, _) in points)
-        chunks = [(i, k, n, r0, min(m, r0 + E2E_ROWS)) for i, (k, n, m) in enumerate(points) for r0 in range(0, m, E2E_ROWS)]
+        rows = args.e2e_rows
+        chunks = [(i, k, n, r0, min(m, r0 + rows)) for i, (k, n, m) in enumerate(points) for r0 in range(0, m, rows)]
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         nslot = 3
-        dbuf = [torch.empty(min(big_in, E2E_ROWS * kmax), dtype=torch.bfloat16, device=dev) for _ in range(nslot)]
+        dbuf = [torch.empty(min(big_in, rows * kmax), dtype=torch.bfloat16, device=dev) for _ in range(nslot)]
         slot_free = [None] * nslot  # compute-done event of the chunk that last read each slot
 
         def e2e_step():
