@@ -71,6 +71,7 @@ struct W4sCfg {
   static constexpr int RING_BYTES = A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES;
   static_assert(RED_WORDS * 4 <= RING_BYTES, "the split-K receive area lives in the ring memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(2 * BN + MS * BM <= 1024, "the epilogue constants fit the 4 KB level-table area");
 };
 
 // 16 bytes into this CTA's shared memory (`addr`: a shared::cta address)
@@ -84,10 +85,11 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_
 
 // The W4A8 epilogue of `n` (<= 8) consecutive accumulators of one row, runtime dtype / mode (the same operations, in the
 // same order, as epilogue_row32: (fp32(acc) * xs) * s_ch or fp32(acc) * (xs * s_ch), rounded to the output dtype, then
-// + bias and a second rounding), stored at column n0 of `orow`.
-__device__ __forceinline__ void w4s_store8(const int32_t (&a)[8], int n, float xsr, const W4sEpi& e, char* orow, int64_t n0,
-                                           bool vec) {
-  if (e.out_dtype == H3B_INT32) {
+// + bias and a second rounding), stored at column n0 of `orow`.  `sch` / `bias`: the channel scales and the bias (as
+// fp32, exact for every bias dtype; null without a bias) of these columns, staged in shared memory.
+__device__ __forceinline__ void w4s_store8(const int32_t (&a)[8], int n, float xsr, const float* sch, const float* bias,
+                                           int out_dtype, int qmode, char* orow, int64_t n0, bool vec) {
+  if (out_dtype == H3B_INT32) {
     int32_t* o = reinterpret_cast<int32_t*>(orow) + n0;
     if (vec) {
       reinterpret_cast<int4*>(o)[0] = make_int4(a[0], a[1], a[2], a[3]);
@@ -99,18 +101,23 @@ __device__ __forceinline__ void w4s_store8(const int32_t (&a)[8], int n, float x
     }
     return;
   }
+  const float4 s0 = reinterpret_cast<const float4*>(sch)[0], s1 = reinterpret_cast<const float4*>(sch)[1];
+  const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (bias) {
+    const float4 b0 = reinterpret_cast<const float4*>(bias)[0], b1 = reinterpret_cast<const float4*>(bias)[1];
+    bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w; bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+  }
   float v[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float s = j < n ? __ldg(e.sch + n0 + j) : 0.f;
     const float f = __int2float_rn(a[j]);
-    v[j] = e.qmode == H3B_QMODE_CK ? __fmul_rn(__fmul_rn(f, xsr), s) : __fmul_rn(f, __fmul_rn(xsr, s));
+    v[j] = qmode == H3B_QMODE_CK ? __fmul_rn(__fmul_rn(f, xsr), sv[j]) : __fmul_rn(f, __fmul_rn(xsr, sv[j]));
   }
-  if (e.out_dtype == H3B_FP32) {
-    if (e.bias) {
+  if (out_dtype == H3B_FP32) {
+    if (bias) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (j < n) v[j] = __fadd_rn(v[j], static_cast<const float*>(e.bias)[n0 + j]);
+      for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], bv[j]);
     }
     float* o = reinterpret_cast<float*>(orow) + n0;
     if (vec) {
@@ -123,16 +130,12 @@ __device__ __forceinline__ void w4s_store8(const int32_t (&a)[8], int n, float x
     }
     return;
   }
-  const bool bf = e.out_dtype == H3B_BF16;
+  const bool bf = out_dtype == H3B_BF16;
   uint16_t h[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     float r = bf ? __bfloat162float(__float2bfloat16_rn(v[j])) : __half2float(__float2half_rn(v[j]));
-    if (e.bias && j < n) {
-      const float b = bf ? __bfloat162float(static_cast<const __nv_bfloat16*>(e.bias)[n0 + j])
-                         : __half2float(static_cast<const __half*>(e.bias)[n0 + j]);
-      r = __fadd_rn(r, b);
-    }
+    if (bias) r = __fadd_rn(r, bv[j]);
     if (bf) {
       const __nv_bfloat16 t = __float2bfloat16_rn(r);
       h[j] = *reinterpret_cast<const uint16_t*>(&t);
@@ -393,38 +396,64 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
     const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
     const bool vec_ok = (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
     const bool ok = *abort_flag == 0;
+    // the epilogue's per-column and per-row constants, staged once in the (now idle) level-table area: channel scales
+    // and bias of the BN columns (zero past N), activation scales of this CTA's rows of each subtile; visible to every
+    // thread after the first cluster barrier below
+    float* e_sch = reinterpret_cast<float*>(lut);  // [BN]
+    float* e_bias = e_sch + BN;                    // [BN]
+    float* e_xs = e_bias + BN;                     // [MS][rows_max]
+    const bool scaled = epi.out_dtype != H3B_INT32, has_bias = scaled && epi.bias != nullptr;
+    for (int i = threadIdx.x; i < BN; i += blockDim.x) {
+      const int64_t n = static_cast<int64_t>(nt) * BN + i;
+      float sv = 0.f, bv = 0.f;
+      if (scaled && n < N) {
+        sv = __ldg(epi.sch + n);
+        if (has_bias)
+          bv = epi.out_dtype == H3B_FP32   ? static_cast<const float*>(epi.bias)[n]
+               : epi.out_dtype == H3B_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(epi.bias)[n])
+                                           : __half2float(static_cast<const __half*>(epi.bias)[n]);
+      }
+      e_sch[i] = sv;
+      e_bias[i] = bv;
+    }
+    for (int i = threadIdx.x; i < MS * rows_max; i += blockDim.x) {
+      const int q = i / rows_max, rl = i - q * rows_max;
+      const int row = row_base + q * BM + r0 + rl;
+      e_xs[i] = (scaled && rl < r1 - r0 && row < M) ? epi.xs[row] : 0.f;
+    }
 #pragma unroll 1
     for (int m0 = 0; m0 < MS; m0 += spr) {
       // before any push: every CTA of the cluster is done with its rings (they receive the pushes) and, after the first
       // round, has read the previous round's subtiles out of its receive area
       cluster_sync();
-      if (warp >= 2 && warp < 6) {
-        // push: TMEM lane (quad * 32 + lane) = subtile row r, 32 columns per load, stored straight into the receive
-        // area of the CTA that owns row r, in this CTA's slot (posted stores, no round trip)
+      {
+        // push: TMEM lane (quad * 32 + lane) = subtile row r; every warp of the CTA takes part, the warps of one lane
+        // quadrant (warp % 4) sharing its 32-column chunks, and stores them straight into the receive area of the CTA
+        // that owns row r, in this CTA's slot (posted stores, no round trip)
         const int quad = warp & 3, r = quad * 32 + lane;
+        const int wq = warp >> 2, nwq = (C::THREADS / 32 - 1 - quad) / 4 + 1;  // this warp's rank in its quadrant
         int owner = (r * splits) / BM;  // the owner p has BM p / S <= r < BM (p + 1) / S
         while (BM * (owner + 1) / splits <= r) ++owner;
         while (BM * owner / splits > r) --owner;
         const uint32_t local = red_u32 + static_cast<uint32_t>(((split * rows_max + (r - BM * owner / splits)) * C::RED_STRIDE) * 4);
         const bool mine = owner == split;  // this CTA's own rows stay on the local path
         const uint32_t dst0 = mine ? local : mapa_rank(local, static_cast<uint32_t>(owner));
+        constexpr int CHUNKS = BN / 32;
 #pragma unroll 1
-        for (int q = 0; q < spr; ++q) {
+        for (int it = wq; it < spr * CHUNKS; it += nwq) {
+          const int q = it / CHUNKS, c = it - q * CHUNKS;
           const uint32_t dst = dst0 + static_cast<uint32_t>(q * sub_words * 4);
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>((m0 + q) * BN + c * 32), v);
-            tmem_ld_wait();
-            if (mine) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>((m0 + q) * BN + c * 32), v);
+          tmem_ld_wait();
+          if (mine) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j)
-                st_shared_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            } else {
+            for (int j = 0; j < 8; ++j)
+              st_shared_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
 #pragma unroll
-              for (int j = 0; j < 8; ++j)
-                st_cluster_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            }
+            for (int j = 0; j < 8; ++j)
+              st_cluster_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           }
         }
       }
@@ -446,9 +475,9 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
             a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
           }
           const int nn = N - n0 < 8 ? static_cast<int>(N - n0) : 8;
-          const float xsr = epi.out_dtype == H3B_INT32 ? 0.f : epi.xs[row];
           char* orow = static_cast<char*>(epi.out) + static_cast<size_t>(row) * static_cast<size_t>(epi.ldo) * osz;
-          w4s_store8(a, nn, xsr, epi, orow, n0, vec_ok && nn == 8);
+          w4s_store8(a, nn, e_xs[(m0 + q) * rows_max + rl], e_sch + 8 * g, has_bias ? e_bias + 8 * g : nullptr,
+                     epi.out_dtype, epi.qmode, orow, n0, vec_ok && nn == 8);
         }
       }
     }
