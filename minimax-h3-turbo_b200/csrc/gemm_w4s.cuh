@@ -1,27 +1,34 @@
 // Kernel KB, small-M form: the W4A8 GEMM for M <= 256 tokens, int4 weight decoded in the producer warps, K split
-// across CTAs so that every SM works although N / BN weight tiles alone would leave many idle.
+// across CTAs so that every SM works although N / 128 weight tiles alone would leave many idle.
 //
-// At small M the weight dominates the bytes and every output tile needs the whole K: one CTA per (N tile) gives
-// 20-108 CTAs for N = 5120-13824 on 148 SMs, each walking all of K.  Here a work unit is (N tile, K range): CTA u owns
-// output columns [BN nt, BN nt + BN) for ALL M rows (up to two 128-row subtiles, so each weight tile is decoded once)
-// and the k-blocks [kb0, kb1) of split s.  Integer partial sums are exact, so splitting K changes no bit of the result.
+// At small M the weight dominates the bytes and every output tile needs the whole K.  Here a work unit is (128 weight
+// rows, K range): CTA u owns output columns [128 nt, 128 nt + 128) for ALL M tokens (up to two 128-token subtiles, so
+// each weight tile is decoded once) and the k-blocks [kb0, kb1) of split s.  Integer partial sums are exact, so
+// splitting K changes no bit of the result.
 //
-//   warp 0      TMA producer of the packed int4 weight tiles (BN x 64 bytes per k-block) into a deep ring (P ring)
-//   warp 6      TMA producer of the activation-code tiles (MS x 128 x 128 bytes per k-block) into the AB ring
-//   warps 7..   decoders: a P stage -> the BN x 128 int8 B tile of an AB stage (level tables + byte permutes, exactly
-//               decode.cuh's levels, 128-byte swizzle), then fence.proxy.async and an arrival per warp
-//   warp 1      MMA issuer: per k-block and M subtile 4 x tcgen05.mma.kind::i8 (K = 32 each) into its TMEM accumulator
+// The tensor core computes the transposed product D[n, m] = sum_k W[n, k] X[m, k]: the decoded weight tile is the
+// MMA's A operand (M = 128 weight rows) and lives in tensor memory, the activation codes are its B operand (N = 128 or
+// 256 tokens) in shared memory.  With the weight as B in shared memory instead, each k-block took two 128 x 128 MMAs
+// whose shared-memory operand reads paced the loop (measured on B200 at 2.9 int8 POP/s over all SMs, against 4.3 for
+// one 128 x 256 MMA with A in TMEM); here the tensor core reads half the shared-memory bytes per multiply-add, and the
+// decoded bytes never pass through shared memory.
+//
+//   warp 0      TMA producer of the packed int4 weight tiles (128 x 64 bytes per k-block, 64-byte swizzle) -> P ring
+//   warp 6      TMA producer of the activation-code tiles (MS x 128 x 128 bytes per k-block) -> A ring
+//   warps 7-22  decoders, four groups of four warps: group g decodes the k-blocks i = g (mod 4), each warp the 32
+//               weight rows of its TMEM lane quadrant (warp % 4), one row per thread (level tables + byte permutes,
+//               exactly decode.cuh's levels), and stores them with tcgen05.st into the group's TMEM stage
+//   warp 1      MMA issuer: per k-block 4 x tcgen05.mma.kind::i8 (K = 32 each, A from TMEM) into the accumulator
 //   warps 2-5   epilogue: wait for the accumulator, then (with every warp of the CTA, after the roles) stage and store.
 //               The S CTAs of one output tile (S K splits; S = 1 included) form a thread-block cluster: CTA p owns 1/S
-//               of the tile's rows, every CTA stores its raw int32 partial sums of each row straight from TMEM into
-//               the owner's (by then idle) ring memory (distributed shared memory stores, posted; its own rows
-//               locally), and after a cluster barrier each owner adds up its rows over the S slots in rank order from
-//               its own shared memory and all its warps apply the W4A8 epilogue (as gemm_sm100.cuh) and store the
-//               output -- no partial sums in HBM, no second kernel, no remote loads.
-// The P ring is separate from (and deeper than) the AB ring, so weight bytes keep streaming from HBM while the tensor
-// core works on earlier k-blocks.  One work unit per CTA; every mbarrier wait bounded (h3b_common.cuh), and every CTA
-// reaches every cluster barrier whatever happened before, so no CTA waits for a peer that left; after the last one no
-// CTA touches another's shared memory.
+//               of the tile's token rows, every CTA stores its raw int32 partial sums straight from TMEM into the
+//               owner's (by then idle) ring memory (distributed shared memory stores, posted; 128 contiguous bytes of
+//               one token row per warp store; its own rows locally), and after a cluster barrier each owner adds up
+//               its rows over the S slots in rank order from its own shared memory and all its warps apply the W4A8
+//               epilogue (as gemm_sm100.cuh) and store the output -- no partial sums in HBM, no second kernel.
+// One work unit per CTA; every mbarrier wait bounded (h3b_common.cuh), and every CTA reaches every cluster barrier
+// whatever happened before, so no CTA waits for a peer that left; after the last one no CTA touches another's shared
+// memory.
 #pragma once
 
 #include "decode.cuh"
@@ -41,46 +48,65 @@ struct W4sEpi {
   int qmode;           // H3B_QMODE_CK / H3B_QMODE_EAGER
 };
 
-template <int BN, int MS>
+constexpr int W4S_BN = 128;  // weight rows (output columns) per CTA: the MMA's M
+
+template <int MS>
 struct W4sCfg {
-  // 16-weight chunks per decoder thread per k-block: 16 decoder warps for BN 128 and 256, 12 for 192 -- enough warps
-  // per scheduler to hide the shared-memory and permute latencies of the decode behind each other
-  static constexpr int CPT = BN == 128 ? 2 : 4;
-  static constexpr int DWARPS = BN * 8 / (32 * CPT);  // decoder warps (a thread owns CPT chunks of one B row)
-  static constexpr int LA = 4;                        // k-blocks of group scales each decoder thread loads ahead
-  static constexpr int A_BYTES = BM * BK;             // one 128-row activation subtile of one k-block
-  static constexpr int B_BYTES = BN * BK;
-  static constexpr int P_BYTES = BN * (BK / 2);
+  static constexpr int BN = W4S_BN;
+  static constexpr int DEPTH = 4;                  // k-blocks decoded ahead: TMEM stages = decoder warp groups
+  static constexpr int DWARPS = 4 * DEPTH;         // one warp per (group, TMEM lane quadrant)
+  static constexpr int LA = 2;                     // look-ahead of a decoder's scale loads, in its own k-blocks
+  static constexpr int A_BYTES = BM * BK;          // one 128-token activation subtile of one k-block
+  static constexpr int P_BYTES = BN * (BK / 2);    // one packed weight tile
   static constexpr int BUDGET = 210 * 1024;
-  // Three rings.  The activation tiles come from L2 with a latency of a few microseconds when every SM streams at
-  // once, so their ring is the deepest the budget allows; the decoded weight tiles are produced in shared memory and
-  // need only double buffering; the packed weight tiles take the rest.
-  static constexpr int A_STAGES = MS == 1 ? 6 : (BN == 128 ? 4 : 3);
-  static constexpr int B_STAGES = MS == 1 && BN == 128 ? 3 : 2;
-  static constexpr int P_LEFT = (BUDGET - A_STAGES * MS * A_BYTES - B_STAGES * B_BYTES) / P_BYTES;
-  static constexpr int P_STAGES = P_LEFT > 10 ? 10 : P_LEFT;
-  static constexpr int TMEM_COLS = MS * BN <= 128 ? 128 : (MS * BN <= 256 ? 256 : 512);
+  // The activation tiles come from L2 with a latency of a few microseconds when every SM streams at once, so they get
+  // 128 KB of ring; the packed weight tiles the rest.
+  static constexpr int A_STAGES = MS == 1 ? 8 : 4;
+  static constexpr int P_LEFT = (BUDGET - A_STAGES * MS * A_BYTES) / P_BYTES;
+  static constexpr int P_STAGES = P_LEFT > 12 ? 12 : P_LEFT;
+  static constexpr int ACC_COLS = MS * BM;         // the accumulator: TMEM lane = weight row, column = token
+  static constexpr int A_COL0 = ACC_COLS;          // then DEPTH decoded stages of 32 columns (128 int8 per row)
+  static constexpr int TMEM_COLS = ACC_COLS + DEPTH * 32 <= 256 ? 256 : 512;
   static constexpr int THREADS = 32 * (7 + DWARPS);
-  static constexpr int SMEM = 1024 + A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES + 4096 + 512;
-  static constexpr uint32_t IDESC = idesc_i8(BM, BN);
-  static_assert(P_STAGES >= 2 && CPT * 32 * DWARPS == BN * 8 && 8 % CPT == 0, "bad small-M GEMM configuration");
-  // the split-K receive area of one 128-row subtile, in the rings: [S][ceil(128 / S)][BN + 4] int32 (rows 16 bytes
+  static constexpr int RING_BYTES = A_STAGES * MS * A_BYTES + P_STAGES * P_BYTES;
+  static constexpr int SMEM = 1024 + RING_BYTES + 4096 + 512;
+  static constexpr uint32_t IDESC = idesc_i8(BN, MS * BM);
+  // the split-K receive area of one 128-token subtile, in the rings: [S][ceil(128 / S)][BN + 4] int32 (rows 16 bytes
   // apart in bank terms); S ceil(128 / S) <= 128 + 7 rows for S <= 8
   static constexpr int RED_STRIDE = BN + 4;
-  static constexpr int RED_WORDS = (BM + 7) * RED_STRIDE;  // one subtile's receive area
-  static constexpr int RING_BYTES = A_STAGES * MS * A_BYTES + B_STAGES * B_BYTES + P_STAGES * P_BYTES;
-  static_assert(RED_WORDS * 4 <= RING_BYTES, "the split-K receive area lives in the ring memory");
+  static constexpr int RED_WORDS = (BM + 7) * RED_STRIDE;
+  static_assert(P_STAGES >= DEPTH + 2, "bad small-M GEMM configuration");
+  static_assert(2 * RED_WORDS * 4 <= RING_BYTES, "the split-K receive areas of both subtiles live in the ring memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(2 * BN + MS * BM <= 1024, "the epilogue constants fit the 4 KB level-table area");
+  static_assert(ACC_COLS + DEPTH * 32 <= TMEM_COLS, "tensor memory");
 };
 
-// 16 bytes into this CTA's shared memory (`addr`: a shared::cta address)
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+// 4 bytes into this CTA's / a cluster CTA's shared memory (`addr`: a shared::cta / shared::cluster address; the
+// remote store is posted)
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
-// 16 bytes into a cluster CTA's shared memory (`addr`: a shared::cluster address; a posted store)
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+// 32 lanes x 8 consecutive 32-bit columns of tensor memory from registers: thread i of the warp writes its lane.
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, int8 x int8 -> int32, one CTA: row r of A in TMEM lane r, its K bytes packed
+// four to a 32-bit column (lowest k in the lowest byte).
+__device__ __forceinline__ void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 // The W4A8 epilogue of `n` (<= 8) consecutive accumulators of one row, runtime dtype / mode (the same operations, in the
@@ -155,26 +181,26 @@ __device__ __forceinline__ void w4s_store8(const int32_t (&a)[8], int n, float x
   }
 }
 
-template <int BN, int MS, int SDT>
-__global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
+template <int MS, int SDT>
+__global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
     gemm_w4s_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
                     const void* __restrict__ s_rel, int64_t lds, const float* __restrict__ codebook, const W4sEpi epi,
                     int M, int N, int K, int splits, int m_tiles) {
-  using C = W4sCfg<BN, MS>;
+  using C = W4sCfg<MS>;
+  constexpr int BN = C::BN;
   constexpr int GROUP = SDT == H3B_FP8_E4M3 ? 16 : 128;
   extern __shared__ __align__(1024) unsigned char w4s_smem[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(w4s_smem) + 1023) & ~uintptr_t(1023));
   unsigned char* sA = smem;                                    // [A_STAGES][MS][A_BYTES]
-  unsigned char* sB = sA + C::A_STAGES * MS * C::A_BYTES;      // [B_STAGES][B_BYTES]
-  unsigned char* sP = sB + C::B_STAGES * C::B_BYTES;           // [P_STAGES][P_BYTES]
+  unsigned char* sP = sA + C::A_STAGES * MS * C::A_BYTES;      // [P_STAGES][P_BYTES]
   uint4* lut = reinterpret_cast<uint4*>(sP + C::P_STAGES * C::P_BYTES);  // fp8: the 256 level tables
   uint64_t* pkfull = reinterpret_cast<uint64_t*>(lut + 256);
   uint64_t* pkempty = pkfull + C::P_STAGES;
   uint64_t* afull = pkempty + C::P_STAGES;
   uint64_t* aempty = afull + C::A_STAGES;
-  uint64_t* bfull = aempty + C::A_STAGES;
-  uint64_t* bempty = bfull + C::B_STAGES;
-  uint64_t* tfull = bempty + C::B_STAGES;
+  uint64_t* dfull = aempty + C::A_STAGES;   // a decoded weight stage in TMEM is complete
+  uint64_t* dempty = dfull + C::DEPTH;      // the MMAs of a decoded stage are done with it
+  uint64_t* tfull = dempty + C::DEPTH;
   uint64_t* mdone = tfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -193,15 +219,15 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::P_STAGES; ++s) {
       mbar_init(&pkfull[s], 1);
-      mbar_init(&pkempty[s], C::DWARPS);
+      mbar_init(&pkempty[s], 4);  // the four quadrant warps of the group that decodes it
     }
     for (int s = 0; s < C::A_STAGES; ++s) {
       mbar_init(&afull[s], 1);
       mbar_init(&aempty[s], 1);
     }
-    for (int s = 0; s < C::B_STAGES; ++s) {
-      mbar_init(&bfull[s], C::DWARPS);
-      mbar_init(&bempty[s], 1);
+    for (int s = 0; s < C::DEPTH; ++s) {
+      mbar_init(&dfull[s], 4);
+      mbar_init(&dempty[s], 1);
     }
     mbar_init(tfull, 1);
     mbar_init(mdone, 1);
@@ -263,25 +289,22 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ------------------------------------------------------ MMA issuer
-      int as = 0, bs = 0;
-      uint32_t aph = 0, bph = 0;
+      int as = 0;
+      uint32_t aph = 0;
       bool ok = true;
       for (int i = 0; i < nkb && ok; ++i) {
-        if (!mbar_wait(&afull[as], aph, abort_flag) || !mbar_wait(&bfull[bs], bph, abort_flag)) { ok = false; break; }
+        const int ds = i % C::DEPTH;
+        const uint32_t dph = static_cast<uint32_t>((i / C::DEPTH) & 1);
+        if (!mbar_wait(&afull[as], aph, abort_flag) || !mbar_wait(&dfull[ds], dph, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t b0 = smem_u32(sB + bs * C::B_BYTES);
+        const uint32_t b0 = smem_u32(sA + as * MS * C::A_BYTES);  // the MS subtiles: one K-major tile of MS x 128 rows
+        const uint32_t a0 = tmem_base + static_cast<uint32_t>(C::A_COL0 + 32 * ds);
 #pragma unroll
-        for (int ms = 0; ms < MS; ++ms) {
-          const uint32_t a0 = smem_u32(sA + (as * MS + ms) * C::A_BYTES);
-#pragma unroll
-          for (int k = 0; k < BK / 32; ++k)
-            mma_i8(tmem_base + static_cast<uint32_t>(ms * BN), smem_desc_sw128(a0 + 32 * k), smem_desc_sw128(b0 + 32 * k),
-                   C::IDESC, (i | k) != 0);
-        }
-        mma_commit(&aempty[as]);  // both slots free once these MMAs complete
-        mma_commit(&bempty[bs]);
+        for (int k = 0; k < BK / 32; ++k)
+          mma_i8_ts(tmem_base, a0 + static_cast<uint32_t>(8 * k), smem_desc_sw128(b0 + 32 * k), C::IDESC, (i | k) != 0);
+        mma_commit(&aempty[as]);  // the activation slot and the decoded stage are free once these MMAs complete
+        mma_commit(&dempty[ds]);
         if (++as == C::A_STAGES) { as = 0; aph ^= 1u; }
-        if (++bs == C::B_STAGES) { bs = 0; bph ^= 1u; }
       }
       if (ok) mma_commit(tfull);
       mma_commit(mdone);
@@ -292,88 +315,81 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
     // warp of the CTA (below)
     mbar_wait(tfull, 0, abort_flag);
   } else {  // -------------------------------------------------------------------------------------- decoders
-    const int dt = threadIdx.x - 224;             // 0 .. 32 DWARPS - 1
-    const int r_loc = (dt * C::CPT) >> 3;         // this thread's row of the B tile
-    const int j0 = (dt * C::CPT) & 7;             // its first 16-weight chunk in the row
-    // group-128 scales: the TPR adjacent lanes of one weight row build its level table together, WPT of the four
-    // table words each, and exchange them by shuffles
-    constexpr int TPR = 8 / C::CPT, WPT = 4 / TPR;
-    float cbm[4 * WPT];  // the codebook entries of this lane's table words
-    if constexpr (SDT != H3B_FP8_E4M3) {
-#pragma unroll
-      for (int e = 0; e < 4 * WPT; ++e) cbm[e] = __ldg(codebook + 4 * WPT * (lane % TPR) + e);
-    }
-    auto table = [&](float sc) -> uint4 {
-      uint32_t mine[WPT];
-#pragma unroll
-      for (int w = 0; w < WPT; ++w)
-        mine[w] = pack4(level_of(cbm[4 * w], sc), level_of(cbm[4 * w + 1], sc), level_of(cbm[4 * w + 2], sc),
-                        level_of(cbm[4 * w + 3], sc));
-      uint32_t tw[4];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) tw[w] = __shfl_sync(0xffffffffu, mine[w % WPT], (lane & ~(TPR - 1)) | (w / WPT));
-      return make_uint4(tw[0], tw[1], tw[2], tw[3]);
-    };
+    const int grp = (warp - 7) >> 2;      // this warp decodes the k-blocks i = grp (mod DEPTH) into TMEM stage grp
+    const int quad = warp & 3;            // its TMEM lane quadrant
+    const int r_loc = quad * 32 + lane;   // this thread's weight row of the tile = its TMEM lane
     const int n = nt * BN + r_loc;
     const bool row_ok = n < N;
     const unsigned char* srow = static_cast<const unsigned char*>(s_rel) +
                                 static_cast<int64_t>(row_ok ? n : 0) * lds * (SDT == H3B_FP8_E4M3 ? 1 : (SDT == H3B_FP32 ? 4 : 2));
-    // this thread's group scales of k-block i: the one scale of its row (group-128 formats, as a float) or the scale
-    // byte of each of its chunks (fp8 group 16); plain global loads, issued LA k-blocks before their use
-    auto load_scales = [&](int i, float& g, uint32_t (&f8)[C::CPT]) {
+    float cb[16];
+    if constexpr (SDT != H3B_FP8_E4M3) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) cb[e] = __ldg(codebook + e);
+    }
+    // the group scales of k-block i: the one scale of this row (group-128 formats, as a float) or its 8 scale bytes
+    // (fp8 group 16); plain global loads, issued LA of this warp's k-blocks before their use
+    auto load_scales = [&](int i, float& g, uint2& f8) {
       const int64_t kbase = static_cast<int64_t>(kb0 + i) * BK;
       if constexpr (SDT == H3B_FP8_E4M3) {
+        uint32_t b[8];
 #pragma unroll
-        for (int c = 0; c < C::CPT; ++c) {
-          const int64_t e0 = kbase + 16 * (j0 + c);
-          f8[c] = (row_ok && i < nkb && e0 < K) ? static_cast<uint32_t>(srow[e0 / GROUP]) : 0u;
+        for (int c = 0; c < 8; ++c) {
+          const int64_t e0 = kbase + 16 * c;
+          b[c] = (row_ok && i < nkb && e0 < K) ? static_cast<uint32_t>(srow[e0 / GROUP]) : 0u;
         }
+        f8 = make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24), b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24));
       } else {
-        const int64_t e0 = kbase + 16 * j0;
-        g = (row_ok && i < nkb && e0 < K) ? scale_at<SDT>(srow, e0 / GROUP) : 0.f;
+        g = (row_ok && i < nkb && kbase < K) ? scale_at<SDT>(srow, kbase / GROUP) : 0.f;
       }
     };
     float sg[C::LA];
-    uint32_t s8[C::LA][C::CPT];
+    uint2 s8[C::LA];
 #pragma unroll
     for (int u = 0; u < C::LA; ++u) {
       sg[u] = 0.f;
-#pragma unroll
-      for (int c = 0; c < C::CPT; ++c) s8[u][c] = 0u;
-      load_scales(u, sg[u], s8[u]);
+      s8[u] = make_uint2(0u, 0u);
+      load_scales(grp + u * C::DEPTH, sg[u], s8[u]);
     }
-    int ps = 0, bs = 0;
-    uint32_t pph = 0, bph = 0;
+    const uint32_t tstage = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(C::A_COL0 + 32 * grp);
+    const int sw = (r_loc >> 1) & 3;  // 64-byte swizzle: 16-byte chunk c of packed row r sits at chunk c ^ ((r >> 1) & 3)
     bool ok = true;
-    for (int i0 = 0; i0 < nkb && ok; i0 += C::LA) {
+    for (int i0 = grp; i0 < nkb && ok; i0 += C::LA * C::DEPTH) {
 #pragma unroll
       for (int u = 0; u < C::LA; ++u) {  // unrolled, so the scale ring stays in registers
-        const int i = i0 + u;
+        const int i = i0 + u * C::DEPTH;
         if (i >= nkb) break;
-        // warp-uniform outcome, so that no lane leaves while the others wait in the table's shuffles
-        const bool got = mbar_wait(&pkfull[ps], pph, abort_flag) && mbar_wait(&bempty[bs], bph ^ 1u, abort_flag);
+        const int ps = i % C::P_STAGES;
+        const uint32_t pph = static_cast<uint32_t>((i / C::P_STAGES) & 1);
+        const uint32_t dph = static_cast<uint32_t>(((i / C::DEPTH) & 1) ^ 1);
+        // warp-uniform outcome: tcgen05.st below is a whole-warp instruction
+        const bool got = mbar_wait(&pkfull[ps], pph, abort_flag) && mbar_wait(&dempty[grp], dph, abort_flag);
         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        tc_fence_after();
         uint4 t = make_uint4(0, 0, 0, 0);
-        if constexpr (SDT != H3B_FP8_E4M3) t = table(sg[u]);
+        if constexpr (SDT != H3B_FP8_E4M3) t = level_table(cb, sg[u]);
         const unsigned char* prow = sP + ps * C::P_BYTES + r_loc * (BK / 2);
-        unsigned char* brow = sB + bs * C::B_BYTES + r_loc * BK;
 #pragma unroll
-        for (int c = 0; c < C::CPT; ++c) {
-          const int j = j0 + c;
-          if constexpr (SDT == H3B_FP8_E4M3) t = lut[s8[u][c]];
-          const uint2 pk = *reinterpret_cast<const uint2*>(prow + 8 * j);
-          const uint2 lo = decode8(pk.x, t), hi = decode8(pk.y, t);
-          *reinterpret_cast<uint4*>(brow + ((j ^ (r_loc & 7)) << 4)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        for (int c = 0; c < 4; ++c) {  // 16 packed bytes = 32 weights = 8 TMEM columns
+          const uint4 pk = *reinterpret_cast<const uint4*>(prow + ((c ^ sw) << 4));
+          uint4 t0 = t, t1 = t;
+          if constexpr (SDT == H3B_FP8_E4M3) {
+            const uint32_t sb = c < 2 ? s8[u].x : s8[u].y;
+            t0 = lut[(sb >> (16 * (c & 1))) & 0xFFu];
+            t1 = lut[(sb >> (16 * (c & 1) + 8)) & 0xFFu];
+          }
+          const uint2 d0 = decode8(pk.x, t0), d1 = decode8(pk.y, t0), d2 = decode8(pk.z, t1), d3 = decode8(pk.w, t1);
+          const uint32_t w[8] = {d0.x, d0.y, d1.x, d1.y, d2.x, d2.y, d3.x, d3.y};
+          tmem_st_32x32b_x8(tstage + static_cast<uint32_t>(8 * c), w);
         }
-        fence_proxy_async_smem();  // the tensor core reads these bytes through the async proxy
+        tmem_st_wait();
+        tc_fence_before();  // the MMA issuer reads these columns after the arrival below
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&bfull[bs]);
+          mbar_arrive(&dfull[grp]);
           mbar_arrive(&pkempty[ps]);
         }
-        if (++ps == C::P_STAGES) { ps = 0; pph ^= 1u; }
-        if (++bs == C::B_STAGES) { bs = 0; bph ^= 1u; }
-        load_scales(i + C::LA, sg[u], s8[u]);
+        load_scales(i + C::LA * C::DEPTH, sg[u], s8[u]);
       }
     }
   }
@@ -382,8 +398,8 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
   __syncthreads();
   {  // -------------------------------------------------------------------- staging, split-K reduction and epilogue
     tc_fence_after();
-    // receive area [source rank][row - first row of this CTA][column]; every ring is idle now (all MMAs and copies
-    // have completed)
+    // receive area [subtile][source rank][token row - first row of this CTA][column]; every ring is idle now (all MMAs
+    // and copies have completed)
     int32_t* red = reinterpret_cast<int32_t*>(sA);
     const uint32_t red_u32 = smem_u32(red);
     const int rows_max = (BM + splits - 1) / splits;
@@ -427,33 +443,38 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
       // round, has read the previous round's subtiles out of its receive area
       cluster_sync();
       {
-        // push: TMEM lane (quad * 32 + lane) = subtile row r; every warp of the CTA takes part, the warps of one lane
-        // quadrant (warp % 4) sharing its 32-column chunks, and stores them straight into the receive area of the CTA
-        // that owns row r, in this CTA's slot (posted stores, no round trip)
-        const int quad = warp & 3, r = quad * 32 + lane;
+        // push: TMEM lane (quad * 32 + lane) = output column n_loc of the tile, TMEM column = token; every warp of the
+        // CTA takes part, the warps of one lane quadrant (warp % 4) sharing its 32-token chunks.  Each token row goes
+        // to the CTA that owns it, into this CTA's slot: for one token the 32 lanes of a warp store 128 contiguous
+        // bytes (posted stores, no round trip); own rows stay local
+        const int quad = warp & 3, n_loc = quad * 32 + lane;
         const int wq = warp >> 2, nwq = (C::THREADS / 32 - 1 - quad) / 4 + 1;  // this warp's rank in its quadrant
-        int owner = (r * splits) / BM;  // the owner p has BM p / S <= r < BM (p + 1) / S
-        while (BM * (owner + 1) / splits <= r) ++owner;
-        while (BM * owner / splits > r) --owner;
-        const uint32_t local = red_u32 + static_cast<uint32_t>(((split * rows_max + (r - BM * owner / splits)) * C::RED_STRIDE) * 4);
-        const bool mine = owner == split;  // this CTA's own rows stay on the local path
-        const uint32_t dst0 = mine ? local : mapa_rank(local, static_cast<uint32_t>(owner));
-        constexpr int CHUNKS = BN / 32;
+        constexpr int CHUNKS = BM / 32;
 #pragma unroll 1
         for (int it = wq; it < spr * CHUNKS; it += nwq) {
           const int q = it / CHUNKS, c = it - q * CHUNKS;
-          const uint32_t dst = dst0 + static_cast<uint32_t>(q * sub_words * 4);
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>((m0 + q) * BN + c * 32), v);
+          uint32_t v[32];  // v[j] = D[n_loc][token 32 c + j of subtile m0 + q]
+          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>((m0 + q) * BM + c * 32), v);
           tmem_ld_wait();
-          if (mine) {
+          const uint32_t qoff = red_u32 + static_cast<uint32_t>((q * sub_words + n_loc) * 4);
+          int owner = 0, rbase = 0, rnext = 0;
+          uint32_t dbase = 0;
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              st_shared_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              st_cluster_v4(dst + static_cast<uint32_t>((c * 32 + 4 * j) * 4), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          for (int j = 0; j < 32; ++j) {
+            const int r = c * 32 + j;  // token row of the subtile
+            if (j == 0 || r >= rnext) {  // warp-uniform: the owner p has BM p / S <= r < BM (p + 1) / S
+              owner = (r * splits) / BM;
+              while (BM * (owner + 1) / splits <= r) ++owner;
+              while (BM * owner / splits > r) --owner;
+              rbase = BM * owner / splits;
+              rnext = BM * (owner + 1) / splits;
+              dbase = owner == split ? qoff : mapa_rank(qoff, static_cast<uint32_t>(owner));
+            }
+            const uint32_t addr = dbase + static_cast<uint32_t>(((split * rows_max + (r - rbase)) * C::RED_STRIDE) * 4);
+            if (owner == split)
+              st_shared_u32(addr, v[j]);
+            else
+              st_cluster_u32(addr, v[j]);
           }
         }
       }
@@ -491,58 +512,71 @@ __global__ void __launch_bounds__(W4sCfg<BN, MS>::THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------------ host side
-// The work split: all M rows per CTA (MS subtiles) or one CTA per 128-row M tile, then the N tile width and the number
-// of K splits S <= 4 (larger clusters measured slower: fewer of them fit the GPCs at once) with the shortest estimated
-// time -- one wave of at most cap[S] CTAs (clusters of S CTAs that can be resident at once; several waves only without
-// a split), each doing ceil(num_kb / S) k-blocks.  The terms, in microseconds, were fitted to %globaltimer stamps per CTA
-// phase and graph-timed sweeps of forced plans on B200 (M = 256; (K, N) = (5120, 5120), (5120, 13824), (13824, 5120) and
-// the official fp8 shapes): a k-block costs 0.45 / 0.6 / 0.8 us for one 128-row subtile and BN = 128 / 192 / 256
-// columns, 0.72 / 0.9 / 1.02 us for two (the decode of the weight tile is the bound; two subtiles share it), stretched
-// when fewer than 64 CTAs run; start-up takes 2 us, and each wave ends with the staging and the epilogue: 8.5 us +
-// 0.026 us per subtile column across a cluster, 3 us + 0.055 us per subtile column without a split (measured; the
-// single-CTA epilogue of a whole 128- or 256-row tile is slower per column than a cluster member's share).
+// The work split: all M rows per CTA (MS subtiles) or one CTA per 128-row M tile, then the number of K splits S <= 4
+// (larger clusters measured slower: fewer of them fit the GPCs at once) with the shortest estimated time -- one wave of
+// at most cap[S] CTAs (clusters of S CTAs that can be resident at once; several waves only without a split), each doing
+// ceil(num_kb / S) k-blocks.  The terms, in microseconds, were fitted to graph-timed sweeps of forced plans on B200
+// (M = 128 and 256; (K, N) = (5120, 5120), (5120, 13824), (13824, 5120) and the official fp8 shapes): a k-block costs
+// PER_KB[MS], stretched when fewer than 64 CTAs run; start-up takes 2 us, and each wave ends with the staging and the
+// epilogue, EPI_SPLIT + EPI_COL per token column with a split, EPI_ONE + EPI_COL1 per token column without.
 struct W4sPlan {
-  int bn, ms, splits;  // N tile, 128-row M subtiles per CTA (1: one CTA per M tile), K splits
+  int bn, ms, splits;  // N tile (always W4S_BN), 128-row M subtiles per CTA (1: one CTA per M tile), K splits
 };
 
 inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, const int (&cap)[9]) {
+  constexpr double PER_KB[3] = {0.0, 0.30, 0.40};
+  constexpr double EPI_SPLIT = 5.0, EPI_COL = 0.02, EPI_ONE = 2.0, EPI_COL1 = 0.02;
   const int64_t num_kb = (K + BK - 1) / BK;
-  W4sPlan best{128, M <= BM ? 1 : 2, 1};
+  const int64_t n_tiles = (N + W4S_BN - 1) / W4S_BN;
+  W4sPlan best{W4S_BN, M <= BM ? 1 : 2, 1};
   double best_t = -1;
   for (int ms : {1, 2}) {
     if (ms == 2 && M <= BM) continue;
     const int64_t m_tiles = ms == 1 ? (M + BM - 1) / BM : 1;
-    for (int bn : {256, 192, 128}) {
-      const int64_t n_tiles = (N + bn - 1) / bn;
-      for (int s = 1; s <= 4 && s <= num_kb; ++s) {
-        if (cap[s] < s) continue;
-        const int64_t units = m_tiles * n_tiles * s;
-        const int64_t waves = (units + cap[s] - 1) / cap[s];
-        if (waves > 1 && s > 1) break;
-        double per_kb = ms == 2 ? (bn == 128 ? 0.72 : bn == 192 ? 0.9 : 1.02) : (bn == 128 ? 0.45 : bn == 192 ? 0.6 : 0.8);
-        if (units < 64) per_kb *= 64.0 / static_cast<double>(units);
-        // every wave pays its k-blocks and its epilogue; start-up once
-        const double epi = s > 1 ? 8.5 + 0.026 * ms * bn : 3.0 + 0.055 * ms * bn;
-        const double t = 2.0 + static_cast<double>(waves) * (((num_kb + s - 1) / s) * per_kb + epi);
-        if (best_t < 0 || t < best_t) {
-          best_t = t;
-          best = W4sPlan{bn, ms, s};
-        }
+    for (int s = 1; s <= 4 && s <= num_kb; ++s) {
+      if (cap[s] < s) continue;
+      const int64_t units = m_tiles * n_tiles * s;
+      const int64_t waves = (units + cap[s] - 1) / cap[s];
+      if (waves > 1 && s > 1) break;
+      double per_kb = PER_KB[ms];
+      if (units < 64) per_kb *= 64.0 / static_cast<double>(units);
+      // every wave pays its k-blocks and its epilogue; start-up once
+      const double epi = s > 1 ? EPI_SPLIT + EPI_COL * ms * BM : EPI_ONE + EPI_COL1 * ms * BM;
+      const double t = 2.0 + static_cast<double>(waves) * (((num_kb + s - 1) / s) * per_kb + epi);
+      if (best_t < 0 || t < best_t) {
+        best_t = t;
+        best = W4sPlan{W4S_BN, ms, s};
       }
     }
   }
   return best;
 }
 
-template <int BN, int MS, int SDT>
+// 2-D uint8 tensor map over the packed weight for this kernel: box 64 bytes x 128 rows, 64-byte swizzle (so that the
+// decoders' 16-byte row reads of one column of chunks spread over all banks), zero fill.
+static int make_map_packed_sw64(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(H3B_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK / 2), static_cast<cuuint32_t>(W4S_BN)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(H3B_ERR_CUDA, "cuTensorMapEncodeTiled (packed, swizzled) failed (code " + std::to_string(int(r)) + ")");
+  return H3B_OK;
+}
+
+template <int MS, int SDT>
 static int w4s_set_attrs() {
-  using C = W4sCfg<BN, MS>;
+  using C = W4sCfg<MS>;
   static std::atomic<unsigned long long> attr_done{0};  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(attr_done.load() & bit)) {
-    const cudaError_t e = cudaFuncSetAttribute(gemm_w4s_kernel<BN, MS, SDT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    const cudaError_t e = cudaFuncSetAttribute(gemm_w4s_kernel<MS, SDT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm w4s)");
     attr_done.fetch_or(bit);
   }
@@ -550,7 +584,7 @@ static int w4s_set_attrs() {
 }
 
 // CTAs that can be resident at once for each cluster size 1..8 (every configuration takes one CTA per SM), queried
-// once per device on the 256-column one-subtile kernel.
+// once per device on the one-subtile kernel.
 template <int SDT>
 static int w4s_capacity(int (&cap)[9]) {
   static std::mutex mu;
@@ -560,15 +594,15 @@ static int w4s_capacity(int (&cap)[9]) {
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
   if (!(done & (1ull << (dev & 63)))) {
-    if (int rc = w4s_set_attrs<256, 1, SDT>()) return rc;
+    if (int rc = w4s_set_attrs<1, SDT>()) return rc;
     int* c = cached[dev & 63];
     c[0] = 0;
     c[1] = num_sms();
     for (int s = 2; s <= 8; ++s) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(static_cast<unsigned>(s), 1, 1);
-      cfg.blockDim = dim3(W4sCfg<256, 1>::THREADS, 1, 1);
-      cfg.dynamicSmemBytes = W4sCfg<256, 1>::SMEM;
+      cfg.blockDim = dim3(W4sCfg<1>::THREADS, 1, 1);
+      cfg.dynamicSmemBytes = W4sCfg<1>::SMEM;
       cudaLaunchAttribute attr;
       attr.id = cudaLaunchAttributeClusterDimension;
       attr.val.clusterDim.x = static_cast<unsigned>(s);
@@ -577,7 +611,7 @@ static int w4s_capacity(int (&cap)[9]) {
       cfg.attrs = &attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, gemm_w4s_kernel<256, 1, SDT>, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_w4s_kernel<1, SDT>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
       }
@@ -589,13 +623,13 @@ static int w4s_capacity(int (&cap)[9]) {
   return 0;
 }
 
-template <int BN, int MS, int SDT>
+template <int MS, int SDT>
 static int w4s_launch_cfg(int splits, const CUtensorMap& ta, const CUtensorMap& tp, const void* s_rel, int64_t lds,
                           const float* codebook, const W4sEpi& epi, int M, int N, int K, cudaStream_t st) {
-  using C = W4sCfg<BN, MS>;
-  if (int rc = w4s_set_attrs<BN, MS, SDT>()) return rc;
+  using C = W4sCfg<MS>;
+  if (int rc = w4s_set_attrs<MS, SDT>()) return rc;
   const int m_tiles = MS == 1 ? (M + BM - 1) / BM : 1;
-  const int units = ((N + BN - 1) / BN) * m_tiles * splits;
+  const int units = ((N + C::BN - 1) / C::BN) * m_tiles * splits;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(units), 1, 1);
   cfg.blockDim = dim3(C::THREADS, 1, 1);
@@ -608,7 +642,7 @@ static int w4s_launch_cfg(int splits, const CUtensorMap& ta, const CUtensorMap& 
   attr.val.clusterDim.z = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_w4s_kernel<BN, MS, SDT>, ta, tp, s_rel, lds, codebook, epi, M, N, K,
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_w4s_kernel<MS, SDT>, ta, tp, s_rel, lds, codebook, epi, M, N, K,
                                            splits, m_tiles);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemm_w4s_kernel)");
   return check_launch("gemm_w4s_kernel");
@@ -622,14 +656,14 @@ int w4s_launch_sdt(const W4sPlan* force, const int8_t* a, int64_t lda, const voi
   if (int rc = w4s_capacity<SDT>(cap)) return rc;
   const W4sPlan plan = force ? *force : w4s_plan(M, N, K, cap);
   if (plan.splits < 1 || plan.splits > 8) return fail(H3B_ERR_ARG, "small-M GEMM: 1 to 8 K splits");
+  if (plan.bn != W4S_BN) return fail(H3B_ERR_ARG, "small-M GEMM: the N tile is 128");
   CUtensorMap ta, tp;
   int rc = make_map(&ta, a, K, M, lda, BM);
   if (rc) return rc;
-  rc = make_map_packed(&tp, q4, K / 2, N, ldq4, plan.bn);
+  rc = make_map_packed_sw64(&tp, q4, K / 2, N, ldq4);
   if (rc) return rc;
-#define H3B_W4S(B, S) if (plan.bn == B && plan.ms == S) return w4s_launch_cfg<B, S, SDT>(plan.splits, ta, tp, s_rel, lds, codebook, epi, M, N, K, st);
-  H3B_W4S(256, 2) H3B_W4S(192, 2) H3B_W4S(128, 2) H3B_W4S(256, 1) H3B_W4S(192, 1) H3B_W4S(128, 1)
-#undef H3B_W4S
+  if (plan.ms == 2) return w4s_launch_cfg<2, SDT>(plan.splits, ta, tp, s_rel, lds, codebook, epi, M, N, K, st);
+  if (plan.ms == 1) return w4s_launch_cfg<1, SDT>(plan.splits, ta, tp, s_rel, lds, codebook, epi, M, N, K, st);
   return fail(H3B_ERR_ARG, "small-M GEMM: unsupported tile plan");
 }
 

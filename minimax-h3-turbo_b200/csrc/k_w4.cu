@@ -65,7 +65,7 @@ int gemm_w4_launch(const int8_t* a, int64_t lda, const void* q4, int64_t ldq4, c
     const W4sPlan* plan = nullptr;
     if (const char* e = getenv("H3B_W4S_PLAN")) {
       int bn = 0, sp = 0, ms = 0;
-      if (sscanf(e, "%d,%d,%d", &bn, &sp, &ms) == 3 && (bn == 128 || bn == 192 || bn == 256) && sp >= 1 && sp <= 8 &&
+      if (sscanf(e, "%d,%d,%d", &bn, &sp, &ms) == 3 && bn == W4S_BN && sp >= 1 && sp <= 8 &&
           sp <= static_cast<int>((K + BK - 1) / BK) && (ms == 1 || (ms == 2 && M <= 2 * BM))) {
         forced = W4sPlan{bn, ms, sp};
         plan = &forced;

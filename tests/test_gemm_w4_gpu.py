@@ -123,10 +123,10 @@ def test_small_m_worst_case_accumulators_are_exact():
     assert int(got.min()) == int(got.max()) == k * 128 * 127
 
 
-@pytest.mark.parametrize("plan", ["256,8,1", "256,2,2", "192,3,2", "128,5,2", "128,7,1", "192,1,2"])
+@pytest.mark.parametrize("plan", ["128,8,1", "128,2,2", "128,3,2", "128,5,2", "128,7,1", "128,1,2", "128,1,1", "128,4,2"])
 def test_small_m_every_tile_plan_is_exact(plan, monkeypatch):
     """Forced tile plans (N tile, K splits = cluster size, M subtiles per CTA) on a ragged problem: two M subtiles, the
-    second almost empty, N not a multiple of any tile, K splits of unequal length -- bit for bit against decode + GEMM."""
+    second almost empty, N not a multiple of the tile, K splits of unequal length -- bit for bit against decode + GEMM."""
     m, n, k = 131, 1000, 3584
     w = synthetic_w4a8(n, k, seed=7, device=DEV)
     g = torch.Generator(device=DEV).manual_seed(11)
