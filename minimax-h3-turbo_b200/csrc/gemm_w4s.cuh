@@ -19,13 +19,14 @@
 //               weight rows of its TMEM lane quadrant (warp % 4), one row per thread (level tables + byte permutes,
 //               exactly decode.cuh's levels), and stores them with tcgen05.st into the group's TMEM stage
 //   warp 1      MMA issuer: per k-block 4 x tcgen05.mma.kind::i8 (K = 32 each, A from TMEM) into the accumulator
-//   warps 2-5   epilogue: wait for the accumulator, then (with every warp of the CTA, after the roles) stage and store.
-//               The S CTAs of one output tile (S K splits; S = 1 included) form a thread-block cluster: CTA p owns 1/S
-//               of the tile's token rows, every CTA stores its raw int32 partial sums straight from TMEM into the
-//               owner's (by then idle) ring memory (distributed shared memory stores, posted; 128 contiguous bytes of
-//               one token row per warp store; its own rows locally), and after a cluster barrier each owner adds up
-//               its rows over the S slots in rank order from its own shared memory and all its warps apply the W4A8
-//               epilogue (as gemm_sm100.cuh) and store the output -- no partial sums in HBM, no second kernel.
+//   warps 2-5   epilogue: stage the channel scales, bias and token scales in shared memory while the main loop runs,
+//               wait for the accumulator, then (with every warp of the CTA, after the roles) apply the W4A8 epilogue
+//               (as gemm_sm100.cuh).  Without a split straight from TMEM to the output.  With S K splits the S CTAs of
+//               one output tile form a thread-block cluster: CTA p owns 1/S of the tile's token rows, every CTA stores
+//               its raw int32 partial sums straight from TMEM into the owner's (by then idle) ring memory (distributed
+//               shared memory stores, posted; 128 contiguous bytes of one token row per warp store; its own rows
+//               locally), and after a cluster barrier each owner adds up its rows over the S slots in rank order from
+//               its own shared memory -- no partial sums in HBM, no second kernel.
 // One work unit per CTA; every mbarrier wait bounded (h3b_common.cuh), and every CTA reaches every cluster barrier
 // whatever happened before, so no CTA waits for a peer that left; after the last one no CTA touches another's shared
 // memory.
@@ -69,7 +70,7 @@ struct W4sCfg {
   static constexpr int TMEM_COLS = ACC_COLS + DEPTH * 32 <= 256 ? 256 : 512;
   static constexpr int THREADS = 32 * (7 + DWARPS);
   static constexpr int RING_BYTES = A_STAGES * MS * A_BYTES + P_STAGES * P_BYTES;
-  static constexpr int SMEM = 1024 + RING_BYTES + 4096 + 512;
+  static constexpr int SMEM = 1024 + RING_BYTES + 4096 + 512 + 2048;  // rings, fp8 level tables, barriers, epilogue constants
   static constexpr uint32_t IDESC = idesc_i8(BN, MS * BM);
   // the split-K receive area of one 128-token subtile, in the rings: [S][ceil(128 / S)][BN + 4] int32 (rows 16 bytes
   // apart in bank terms); S ceil(128 / S) <= 128 + 7 rows for S <= 8
@@ -78,7 +79,7 @@ struct W4sCfg {
   static_assert(P_STAGES >= DEPTH + 2, "bad small-M GEMM configuration");
   static_assert(2 * RED_WORDS * 4 <= RING_BYTES, "the split-K receive areas of both subtiles live in the ring memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
-  static_assert(2 * BN + MS * BM <= 1024, "the epilogue constants fit the 4 KB level-table area");
+  static_assert((2 * BN + MS * BM) * 4 <= 2048, "the epilogue constants");
   static_assert(ACC_COLS + DEPTH * 32 <= TMEM_COLS, "tensor memory");
 };
 
@@ -181,6 +182,31 @@ __device__ __forceinline__ void w4s_store8(const int32_t (&a)[8], int n, float x
   }
 }
 
+// The same epilogue for one accumulator: column n of `orow`, channel scale `s`, bias `b` (used when `bias`).
+__device__ __forceinline__ void w4s_store1(int32_t a, float xsr, float s, float b, bool bias, int out_dtype, int qmode,
+                                           char* orow, int64_t n) {
+  if (out_dtype == H3B_INT32) {
+    reinterpret_cast<int32_t*>(orow)[n] = a;
+    return;
+  }
+  const float f = __int2float_rn(a);
+  float v = qmode == H3B_QMODE_CK ? __fmul_rn(__fmul_rn(f, xsr), s) : __fmul_rn(f, __fmul_rn(xsr, s));
+  if (out_dtype == H3B_FP32) {
+    if (bias) v = __fadd_rn(v, b);
+    reinterpret_cast<float*>(orow)[n] = v;
+    return;
+  }
+  if (out_dtype == H3B_BF16) {
+    float r = __bfloat162float(__float2bfloat16_rn(v));
+    if (bias) r = __fadd_rn(r, b);
+    reinterpret_cast<__nv_bfloat16*>(orow)[n] = __float2bfloat16_rn(r);
+  } else {
+    float r = __half2float(__float2half_rn(v));
+    if (bias) r = __fadd_rn(r, b);
+    reinterpret_cast<__half*>(orow)[n] = __float2half_rn(r);
+  }
+}
+
 template <int MS, int SDT>
 __global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
     gemm_w4s_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
@@ -204,6 +230,7 @@ __global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
   uint64_t* mdone = tfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* econst = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(lut) + 4096 + 512);  // epilogue constants
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = (N + BN - 1) / BN;
@@ -311,6 +338,34 @@ __global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
       mbar_wait_drain(mdone, 0);
     }
   } else if (warp < 6) {  // ------------------------------------------------------------------- epilogue
+    // while the main loop runs: stage the epilogue's constants -- channel scales and bias (as fp32, exact for every bias
+    // dtype) of the BN columns, zero past N; activation scales of this CTA's token rows of each subtile
+    {
+      const int rows_max = (BM + splits - 1) / splits;
+      const int r0 = BM * split / splits, r1 = BM * (split + 1) / splits;
+      float* e_sch = econst;
+      float* e_bias = e_sch + BN;
+      float* e_xs = e_bias + BN;
+      const bool scaled = epi.out_dtype != H3B_INT32, has_bias = scaled && epi.bias != nullptr;
+      for (int i = threadIdx.x - 64; i < BN; i += 128) {
+        const int64_t n = static_cast<int64_t>(nt) * BN + i;
+        float sv = 0.f, bv = 0.f;
+        if (scaled && n < N) {
+          sv = __ldg(epi.sch + n);
+          if (has_bias)
+            bv = epi.out_dtype == H3B_FP32   ? static_cast<const float*>(epi.bias)[n]
+                 : epi.out_dtype == H3B_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(epi.bias)[n])
+                                             : __half2float(static_cast<const __half*>(epi.bias)[n]);
+        }
+        e_sch[i] = sv;
+        e_bias[i] = bv;
+      }
+      for (int i = threadIdx.x - 64; i < MS * rows_max; i += 128) {
+        const int q = i / rows_max, rl = i - q * rows_max;
+        const int row = row_base + q * BM + r0 + rl;
+        e_xs[i] = (scaled && rl < r1 - r0 && row < M) ? epi.xs[row] : 0.f;
+      }
+    }
     // the accumulator is complete once the last MMA has committed; the epilogue proper runs after the roles, with every
     // warp of the CTA (below)
     mbar_wait(tfull, 0, abort_flag);
@@ -412,31 +467,37 @@ __global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
     const size_t osz = epi.out_dtype == H3B_FP32 || epi.out_dtype == H3B_INT32 ? 4 : 2;
     const bool vec_ok = (epi.ldo % (16 / static_cast<int64_t>(osz))) == 0 && (reinterpret_cast<uintptr_t>(epi.out) & 15) == 0;
     const bool ok = *abort_flag == 0;
-    // the epilogue's per-column and per-row constants, staged once in the (now idle) level-table area: channel scales
-    // and bias of the BN columns (zero past N), activation scales of this CTA's rows of each subtile; visible to every
-    // thread after the first cluster barrier below
-    float* e_sch = reinterpret_cast<float*>(lut);  // [BN]
-    float* e_bias = e_sch + BN;                    // [BN]
-    float* e_xs = e_bias + BN;                     // [MS][rows_max]
-    const bool scaled = epi.out_dtype != H3B_INT32, has_bias = scaled && epi.bias != nullptr;
-    for (int i = threadIdx.x; i < BN; i += blockDim.x) {
-      const int64_t n = static_cast<int64_t>(nt) * BN + i;
-      float sv = 0.f, bv = 0.f;
-      if (scaled && n < N) {
-        sv = __ldg(epi.sch + n);
-        if (has_bias)
-          bv = epi.out_dtype == H3B_FP32   ? static_cast<const float*>(epi.bias)[n]
-               : epi.out_dtype == H3B_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(epi.bias)[n])
-                                           : __half2float(static_cast<const __half*>(epi.bias)[n]);
+    // the epilogue's constants, staged by the epilogue warps during the main loop
+    const float* e_sch = econst;
+    const float* e_bias = e_sch + BN;
+    const float* e_xs = e_bias + BN;
+    const bool has_bias = epi.out_dtype != H3B_INT32 && epi.bias != nullptr;
+    const int quad = warp & 3, n_loc = quad * 32 + lane;  // this thread's TMEM lane = output column of the tile
+    const int wq = warp >> 2, nwq = (C::THREADS / 32 - 1 - quad) / 4 + 1;  // this warp's rank in its lane quadrant
+    constexpr int CHUNKS = BM / 32;
+    if (splits == 1) {
+      // one split: the accumulator is the result; every warp applies the epilogue straight from TMEM, the warps of one
+      // lane quadrant sharing its 32-token chunks, one token row of 32 output columns per warp store
+      const int64_t n = static_cast<int64_t>(nt) * BN + n_loc;
+      const float sv = e_sch[n_loc], bv = e_bias[n_loc];
+#pragma unroll 1
+      for (int it = wq; it < MS * CHUNKS; it += nwq) {
+        const int q = it / CHUNKS, c = it - q * CHUNKS;
+        uint32_t v[32];  // v[j] = D[n_loc][token 32 c + j of subtile q]
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(q * BM + c * 32), v);
+        tmem_ld_wait();
+        if (ok && n < N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int row = row_base + q * BM + c * 32 + j;
+            if (row < M)
+              w4s_store1(static_cast<int32_t>(v[j]), e_xs[q * rows_max + c * 32 + j], sv, bv, has_bias, epi.out_dtype,
+                         epi.qmode, static_cast<char*>(epi.out) + static_cast<size_t>(row) * static_cast<size_t>(epi.ldo) * osz, n);
+          }
+        }
+        __syncwarp();
       }
-      e_sch[i] = sv;
-      e_bias[i] = bv;
-    }
-    for (int i = threadIdx.x; i < MS * rows_max; i += blockDim.x) {
-      const int q = i / rows_max, rl = i - q * rows_max;
-      const int row = row_base + q * BM + r0 + rl;
-      e_xs[i] = (scaled && rl < r1 - r0 && row < M) ? epi.xs[row] : 0.f;
-    }
+    } else {
 #pragma unroll 1
     for (int m0 = 0; m0 < MS; m0 += spr) {
       // before any push: every CTA of the cluster is done with its rings (they receive the pushes) and, after the first
@@ -447,9 +508,6 @@ __global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
         // CTA takes part, the warps of one lane quadrant (warp % 4) sharing its 32-token chunks.  Each token row goes
         // to the CTA that owns it, into this CTA's slot: for one token the 32 lanes of a warp store 128 contiguous
         // bytes (posted stores, no round trip); own rows stay local
-        const int quad = warp & 3, n_loc = quad * 32 + lane;
-        const int wq = warp >> 2, nwq = (C::THREADS / 32 - 1 - quad) / 4 + 1;  // this warp's rank in its quadrant
-        constexpr int CHUNKS = BM / 32;
 #pragma unroll 1
         for (int it = wq; it < spr * CHUNKS; it += nwq) {
           const int q = it / CHUNKS, c = it - q * CHUNKS;
@@ -457,21 +515,30 @@ __global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
           tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>((m0 + q) * BM + c * 32), v);
           tmem_ld_wait();
           const uint32_t qoff = red_u32 + static_cast<uint32_t>((q * sub_words + n_loc) * 4);
-          int owner = 0, rbase = 0, rnext = 0;
-          uint32_t dbase = 0;
+          // the chunk's 32 token rows belong to at most three owners (S <= 8: at least 16 rows each): o0, o0 + 1 from
+          // row j1 on, o0 + 2 from row j2 on; base[k] + j RS 4 is row j's address in owner o0 + k's slot of this CTA
+          const int c0 = c * 32;
+          int o0 = (c0 * splits) / BM;  // the owner p has BM p / S <= r < BM (p + 1) / S
+          while (BM * (o0 + 1) / splits <= c0) ++o0;
+          while (BM * o0 / splits > c0) --o0;
+          const int j1 = BM * (o0 + 1) / splits - c0, j2 = BM * (o0 + 2) / splits - c0;
+          uint32_t base[3];
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            const int o = o0 + k;
+            base[k] = 0;
+            if (o < splits) {
+              const int rf = max(c0, BM * o / splits);  // the owner's first row in this chunk
+              const uint32_t first = qoff + static_cast<uint32_t>(((split * rows_max + rf - BM * o / splits) * C::RED_STRIDE) * 4);
+              base[k] = (o == split ? first : mapa_rank(first, static_cast<uint32_t>(o))) -
+                        static_cast<uint32_t>((rf - c0) * C::RED_STRIDE * 4);
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int r = c * 32 + j;  // token row of the subtile
-            if (j == 0 || r >= rnext) {  // warp-uniform: the owner p has BM p / S <= r < BM (p + 1) / S
-              owner = (r * splits) / BM;
-              while (BM * (owner + 1) / splits <= r) ++owner;
-              while (BM * owner / splits > r) --owner;
-              rbase = BM * owner / splits;
-              rnext = BM * (owner + 1) / splits;
-              dbase = owner == split ? qoff : mapa_rank(qoff, static_cast<uint32_t>(owner));
-            }
-            const uint32_t addr = dbase + static_cast<uint32_t>(((split * rows_max + (r - rbase)) * C::RED_STRIDE) * 4);
-            if (owner == split)
+            const int k = (j >= j1) + (j >= j2);  // warp-uniform
+            const uint32_t addr = (k == 0 ? base[0] : (k == 1 ? base[1] : base[2])) + static_cast<uint32_t>(j * C::RED_STRIDE * 4);
+            if (o0 + k == split)
               st_shared_u32(addr, v[j]);
             else
               st_cluster_u32(addr, v[j]);
@@ -502,6 +569,7 @@ __global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
         }
       }
     }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -513,19 +581,20 @@ __global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
 
 // ------------------------------------------------------------------------------------------------ host side
 // The work split: all M rows per CTA (MS subtiles) or one CTA per 128-row M tile, then the number of K splits S <= 4
-// (larger clusters measured slower: fewer of them fit the GPCs at once) with the shortest estimated time -- one wave of
-// at most cap[S] CTAs (clusters of S CTAs that can be resident at once; several waves only without a split), each doing
+// (larger clusters measured slower: fewer of them fit the GPCs at once) with the shortest estimated time -- waves of at
+// most cap[S] CTAs (clusters of S CTAs that can be resident at once; several waves only without a split), each doing
 // ceil(num_kb / S) k-blocks.  The terms, in microseconds, were fitted to graph-timed sweeps of forced plans on B200
-// (M = 128 and 256; (K, N) = (5120, 5120), (5120, 13824), (13824, 5120) and the official fp8 shapes): a k-block costs
-// PER_KB[MS], stretched when fewer than 64 CTAs run; start-up takes 2 us, and each wave ends with the staging and the
-// epilogue, EPI_SPLIT + EPI_COL per token column with a split, EPI_ONE + EPI_COL1 per token column without.
+// (M = 128 and 256; (K, N) = (5120, 5120), (5120, 13824), (13824, 5120) with fp16 group scales and the official fp8
+// shapes): a k-block costs 0.45 us with group-128 scales and about 0.62 us with fp8 group-16 scales (a level table per 16
+// weights), for one or two 128-token subtiles alike (the decode paces it, not the tensor core), whatever the number of
+// CTAs; start-up takes 2 us; each wave ends with the epilogue, 3.7 + 2.0 MS us without a split (straight from TMEM)
+// and 4.2 + 4.0 MS us with one (cluster barriers, the push of the partial sums, the reduction).
 struct W4sPlan {
   int bn, ms, splits;  // N tile (always W4S_BN), 128-row M subtiles per CTA (1: one CTA per M tile), K splits
 };
 
-inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, const int (&cap)[9]) {
-  constexpr double PER_KB[3] = {0.0, 0.30, 0.40};
-  constexpr double EPI_SPLIT = 5.0, EPI_COL = 0.02, EPI_ONE = 2.0, EPI_COL1 = 0.02;
+inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, bool fp8_scales, const int (&cap)[9]) {
+  const double per_kb = fp8_scales ? 0.62 : 0.45;
   const int64_t num_kb = (K + BK - 1) / BK;
   const int64_t n_tiles = (N + W4S_BN - 1) / W4S_BN;
   W4sPlan best{W4S_BN, M <= BM ? 1 : 2, 1};
@@ -538,10 +607,7 @@ inline W4sPlan w4s_plan(int64_t M, int64_t N, int64_t K, const int (&cap)[9]) {
       const int64_t units = m_tiles * n_tiles * s;
       const int64_t waves = (units + cap[s] - 1) / cap[s];
       if (waves > 1 && s > 1) break;
-      double per_kb = PER_KB[ms];
-      if (units < 64) per_kb *= 64.0 / static_cast<double>(units);
-      // every wave pays its k-blocks and its epilogue; start-up once
-      const double epi = s > 1 ? EPI_SPLIT + EPI_COL * ms * BM : EPI_ONE + EPI_COL1 * ms * BM;
+      const double epi = s > 1 ? 4.2 + 4.0 * ms : 3.7 + 2.0 * ms;
       const double t = 2.0 + static_cast<double>(waves) * (((num_kb + s - 1) / s) * per_kb + epi);
       if (best_t < 0 || t < best_t) {
         best_t = t;
@@ -654,7 +720,7 @@ int w4s_launch_sdt(const W4sPlan* force, const int8_t* a, int64_t lda, const voi
                    int64_t lds, const float* codebook, const W4sEpi& epi, int M, int N, int K, cudaStream_t st) {
   int cap[9];
   if (int rc = w4s_capacity<SDT>(cap)) return rc;
-  const W4sPlan plan = force ? *force : w4s_plan(M, N, K, cap);
+  const W4sPlan plan = force ? *force : w4s_plan(M, N, K, SDT == H3B_FP8_E4M3, cap);
   if (plan.splits < 1 || plan.splits > 8) return fail(H3B_ERR_ARG, "small-M GEMM: 1 to 8 K splits");
   if (plan.bn != W4S_BN) return fail(H3B_ERR_ARG, "small-M GEMM: the N tile is 128");
   CUtensorMap ta, tp;
