@@ -67,7 +67,8 @@ def _worker(rank, world, port, q, exchange, groups):
         block = blk.DiTBlock(HEADS, HD, linear=dense, kv_exchange=exchange, kv_groups=groups, ops=tops.TorchOps())
         y = block(x[a:b].clone(), w, mod, _segments(a, b), cos[a:b], sin[a:b], spec)
         full = blk.gather_rows(y, spec)
-        q.put((rank, ok_gather, full))
+        # by value (numpy), not as a torch tensor shared through a file descriptor: that handle dies with the worker
+        q.put((rank, ok_gather, full.numpy().copy()))
     finally:
         dist.destroy_process_group()
 
@@ -90,6 +91,7 @@ def test_sharded_block_equals_unsharded(world, exchange, groups):
         p.join(timeout=60)
         assert p.exitcode == 0
     for rank, ok_gather, full in res:
+        full = torch.from_numpy(full)
         assert ok_gather
         assert torch.allclose(full, ref, rtol=1e-5, atol=1e-5), (rank, (full - ref).abs().max())
 
@@ -103,7 +105,7 @@ def _tiny_worker(rank, world, port, q, exchange, n):
         spec = blk.ShardSpec(a, b, n, dist.group.WORLD, world, rank)
         block = blk.DiTBlock(HEADS, HD, linear=dense, kv_exchange=exchange, ops=tops.TorchOps())
         y = block(x[a:b].clone(), w, mod, [(0, b - a, 0)] if b > a else [], cos[a:b], sin[a:b], spec)
-        q.put((rank, blk.gather_rows(y, spec)))
+        q.put((rank, blk.gather_rows(y, spec).numpy().copy()))
     finally:
         dist.destroy_process_group()
 
@@ -125,6 +127,7 @@ def test_fewer_tokens_than_ranks(exchange):
         p.join(timeout=60)
         assert p.exitcode == 0
     for rank, full in res:
+        full = torch.from_numpy(full)
         assert torch.isfinite(full).all()
         assert torch.allclose(full, ref, rtol=1e-5, atol=1e-5), (rank, (full - ref).abs().max())
 
