@@ -1244,7 +1244,7 @@ def run_sweep(args, rank, world, local):
         line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": t_max_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "int8", "data": "synthetic", "config": config_dict(args.ms, world),
-                "roofline": {"bound": "tensor", "kernel": "int8 GEMM (gemm_i8_pair_kernel for large M, gemm_w4_kernel with "
+                "roofline": {"bound": "tensor", "kernel": "int8 GEMM (gemm_i8_pair_kernel for large M, gemm_w4s_kernel with "
                                                            "the int4 decode for small M)", "achieved": gemm_tops, "peak": int8_peak,
                              "unit": "TOPS", "frac": gemm_tops / int8_peak, "traffic": traffic,
                              "peak_note": f"int8 dense = 2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s burst)",
