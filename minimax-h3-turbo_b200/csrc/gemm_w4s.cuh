@@ -91,6 +91,13 @@ __device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
 __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
+// 32 lanes x 8 consecutive 32-bit columns of tensor memory into registers: thread i of the warp gets its lane's.
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
 // 32 lanes x 8 consecutive 32-bit columns of tensor memory from registers: thread i of the warp writes its lane.
 __device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(r[0]),
@@ -480,18 +487,20 @@ __global__ void __launch_bounds__(W4sCfg<MS>::THREADS, 1)
       // lane quadrant sharing its 32-token chunks, one token row of 32 output columns per warp store
       const int64_t n = static_cast<int64_t>(nt) * BN + n_loc;
       const float sv = e_sch[n_loc], bv = e_bias[n_loc];
+      // (8 tokens per TMEM load and a rolled loop over them: the unrolled body stays small enough for the instruction
+      // cache, which a fully unrolled 32-token body did not)
 #pragma unroll 1
-      for (int it = wq; it < MS * CHUNKS; it += nwq) {
-        const int q = it / CHUNKS, c = it - q * CHUNKS;
-        uint32_t v[32];  // v[j] = D[n_loc][token 32 c + j of subtile q]
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(q * BM + c * 32), v);
+      for (int it = wq; it < MS * CHUNKS * 4; it += nwq) {
+        const int q = it / (CHUNKS * 4), t0 = (it - q * CHUNKS * 4) * 8;  // subtile, first token of the 8
+        uint32_t v[8];  // v[j] = D[n_loc][token t0 + j of subtile q]
+        tmem_ld_32x32b_x8(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(q * BM + t0), v);
         tmem_ld_wait();
         if (ok && n < N) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int row = row_base + q * BM + c * 32 + j;
+          for (int j = 0; j < 8; ++j) {
+            const int row = row_base + q * BM + t0 + j;
             if (row < M)
-              w4s_store1(static_cast<int32_t>(v[j]), e_xs[q * rows_max + c * 32 + j], sv, bv, has_bias, epi.out_dtype,
+              w4s_store1(static_cast<int32_t>(v[j]), e_xs[q * rows_max + t0 + j], sv, bv, has_bias, epi.out_dtype,
                          epi.qmode, static_cast<char*>(epi.out) + static_cast<size_t>(row) * static_cast<size_t>(epi.ldo) * osz, n);
           }
         }
