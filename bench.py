@@ -44,12 +44,12 @@ MS = [256, 2048, 16384, 65536]
 METRIC = "W4A8 qlinear int8 TOPS"
 WORKLOADS = ("sweep", "block", "stream", "longseq")
 # (K, N, M) -> DRAM bytes read + written by that point's GEMM launch (ncu, one capture of the sweep's launches)
-GEMM_DRAM_BYTES = {(5120, 5120, 256): 14924288, (5120, 5120, 2048): 36766976 + 3584,
-                   (5120, 5120, 16384): 197776384 + 148345344, (5120, 5120, 65536): 775971328 + 657958144,
-                   (5120, 13824, 256): 37938944, (5120, 13824, 2048): 85350656 + 23901184,
-                   (5120, 13824, 16384): 341905152 + 416511232, (5120, 13824, 65536): 2575765504 + 1780960000,
-                   (13824, 5120, 256): 40126976, (13824, 5120, 2048): 154039808 + 8496896,
-                   (13824, 5120, 16384): 1172404224 + 171744768, (13824, 5120, 65536): 10836395520 + 738850816}
+GEMM_DRAM_BYTES = {(5120, 5120, 256): 14918400, (5120, 5120, 2048): 36766976 + 5376,
+                   (5120, 5120, 16384): 197843968 + 149336576, (5120, 5120, 65536): 704727296 + 654303744,
+                   (5120, 13824, 256): 37935616, (5120, 13824, 2048): 85519360 + 23642368,
+                   (5120, 13824, 16384): 332693504 + 413625088, (5120, 13824, 65536): 1164723200 + 1776166144,
+                   (13824, 5120, 256): 40125696, (13824, 5120, 2048): 155100672 + 8222720,
+                   (13824, 5120, 16384): 1039225600 + 160625152, (13824, 5120, 65536): 4936572672 + 723166976}
 HID, HEADS, HEAD_DIM, FFN = 5120, 40, 128, 13824  # DiT width, attention heads x head dim, SwiGLU width
 BLOCK_LINEARS = [(HID, 3 * HID), (HID, HID), (HID, 2 * FFN), (FFN, HID)]  # (K, N): qkv, out, fc1, fc2 (SwiGLU input)
 BLOCK_OPS_PER_TOKEN = sum(2.0 * k * n for k, n in BLOCK_LINEARS)  # 634.4 M
