@@ -57,7 +57,8 @@ struct W4sCfg {
   static constexpr int DEPTH = 3;                  // k-blocks decoded ahead: TMEM stages = decoder warp groups
                                                    // (3 measured 1-4 % faster than 4 and than 2)
   static constexpr int DWARPS = 4 * DEPTH;         // one warp per (group, TMEM lane quadrant)
-  static constexpr int LA = 2;                     // look-ahead of a decoder's scale loads, in its own k-blocks
+  static constexpr int LA = 1;                     // look-ahead of a decoder's scale loads, in its own k-blocks
+                                                   // (1 measured 0-3 % faster than 2 and 3)
   static constexpr int A_BYTES = BM * BK;          // one 128-token activation subtile of one k-block
   static constexpr int P_BYTES = BN * (BK / 2);    // one packed weight tile
   static constexpr int BUDGET = 210 * 1024;
